@@ -1,0 +1,490 @@
+"""Benchmark of the W4A16 SwiGLU FFN path (BASELINE.json metric: FFN tokens/s, with decode HBM GB/s
+and prefill TFLOP/s as the roofline terms), one process per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload cfgX] [--m M] [--impl hmb|reference]
+
+Workloads (seeded synthetic weights and activations; no dataset exists):
+  cfg0  Llama-3.2-1B FFN layer (H 2048, I 8192), decode, M = 1
+  cfg1  the same layer, prefill, M in {128, 512, 2048}; default M = 2048        <- default
+  cfg2  Llama-3.1-8B FFN stack, 32 layers (H 4096, I 14336), M in {1, 8, 32, 4096}
+  cfg3  Qwen2.5-14B FFN stack, 48 layers (H 5120, I 13824), M in {1, 4096}
+  cfg4  Llama-3-70B FFN stack, 80 layers (H 8192, I 28672), M in {1, 4, 16, 64, 8192}
+A step is one pass of M tokens through the workload's layers (each layer gets its own fresh
+normalised input, as the activations between FFN layers pass through a norm). With N > 1 the
+layers are tensor-partitioned across the ranks (gate/up column-, down row-parallel, one NCCL
+all-reduce per layer): total work is fixed, "scaling": "strong".
+
+Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events on the stream that
+runs it; a >L2 buffer is written between steps when the workload's weights fit in L2. Barrier +
+synchronize on both sides; rank 0 prints the max over ranks.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+CONFIGS = {
+    "cfg0": dict(model="llama3.2-1b-ffn", hidden=2048, inter=8192, layers=1, ms=[1], m=1),
+    "cfg1": dict(model="llama3.2-1b-ffn", hidden=2048, inter=8192, layers=1, ms=[128, 512, 2048], m=2048),
+    "cfg2": dict(model="llama3.1-8b-ffn-stack", hidden=4096, inter=14336, layers=32, ms=[1, 8, 32, 4096], m=1),
+    "cfg3": dict(model="qwen2.5-14b-ffn-stack", hidden=5120, inter=13824, layers=48, ms=[1, 4096], m=1),
+    "cfg4": dict(model="llama3-70b-ffn-stack", hidden=8192, inter=28672, layers=80, ms=[1, 4, 16, 64, 8192], m=1),
+}
+L2_BYTES = 126 * 2**20
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+BYTES_PER_WEIGHT = 4352 / 8192
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="cfg1", choices=sorted(CONFIGS))
+    ap.add_argument("--m", type=int, default=0, help="tokens per step (default: the workload's)")
+    ap.add_argument("--layers", type=int, default=0, help="override the layer count (testing only)")
+    ap.add_argument("--impl", default="hmb", choices=["hmb", "reference"])
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--cpu-sample-s", type=float, default=10.0)
+    return ap.parse_args()
+
+
+def workload(args):
+    c = dict(CONFIGS[args.workload])
+    c["m"] = args.m or c["m"]
+    if args.layers:
+        c["layers"] = args.layers
+    c["name"] = args.workload
+    return c
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {k: float(p[k]) for k in ("hbm_gbs", "bf16_tflops", "bf16_tflops_sustained")}, "measured"
+    except (OSError, KeyError, ValueError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def layer_bytes(h, n, m):
+    """Algorithmic HBM bytes of one FFN layer (all of its n channels): packed weights once, x in, y out."""
+    return 3 * h * n * BYTES_PER_WEIGHT + 2 * m * h * 2
+
+
+def layer_flops(h, n, m):
+    return 6.0 * m * h * n
+
+
+# ---- clocks during the timed region (NVML, polled from a thread) ------------------------------------
+
+class ClockSampler:
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4,
+               "hw_power_brake_slowdown": 0x80}
+
+    def __init__(self, device, period_s=0.005):
+        self.period = period_s
+        self.samples, self.reasons = [], set()
+        self._stop = threading.Event()
+        self.max_mhz = None
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            # The NVML handle of this CUDA device, matched by UUID (CUDA_VISIBLE_DEVICES remaps indices).
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            self.h = None
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                h = pynvml.nvmlDeviceGetHandleByIndex(i)
+                u = pynvml.nvmlDeviceGetUUID(h)
+                u = u.decode() if isinstance(u, bytes) else u
+                if u.replace("GPU-", "") == uuid.replace("GPU-", ""):
+                    self.h = h
+            if self.h is None:
+                raise RuntimeError("device not found in NVML")
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # no NVML: the line says so
+            self.nv = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for name, bit in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.nv is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.nv is not None:
+            self._t.join()
+
+    def summary(self):
+        if self.nv is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"], "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---- the product arm -----------------------------------------------------------------------------------
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def run_hmb(args):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import heteromega_b200 as H
+    from heteromega_b200.stack import FfnStack
+    from heteromega_b200.tensor_parallel import TensorParallelFfn
+    from heteromega_b200.weights import synthetic_packed_device
+
+    world, rank, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    wl = workload(args)
+    h, inter, L, m = wl["hidden"], wl["inter"], wl["layers"], wl["m"]
+
+    # Weights: layer l drawn on the device from seed 1000 + l; with N > 1 each rank keeps its shard.
+    tp = TensorParallelFfn(h, inter, rank=rank, world=world) if world > 1 else None
+    layers = []
+    gen = torch.Generator(device=dev)
+    for l in range(L):
+        gen.manual_seed(1000 + l)
+        g = synthetic_packed_device(h, inter, dev, gen)
+        u = synthetic_packed_device(h, inter, dev, gen)
+        d = synthetic_packed_device(inter, h, dev, gen)
+        if tp is not None:
+            tp.add_layer(g, u, d)
+        else:
+            layers.append(H.slice_packed_ffn(g, u, d, h, inter, 0, inter, H.GateUpLayout.kInterleaved))
+        del g, u, d
+    torch.cuda.synchronize()
+    stack = FfnStack(layers, h, dev, tp=tp)
+    n_local = stack.layers[0].channels()
+
+    # Activations: fresh N(0, 1) input per layer (seed 7), resident in HBM.
+    gen.manual_seed(7)
+    x_all = torch.randn(L, m, h, device=dev, generator=gen).to(torch.bfloat16)
+    weights_local = sum(w.gate_up.numel() + w.down.numel() for w in stack.layers)
+    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev) if weights_local < 2 * L2_BYTES else None
+
+    use_graph = not args.no_graph
+    if use_graph:
+        graph, gx, gy = stack.graph(m)
+        gx.copy_(x_all)
+        step = graph.replay
+    else:
+        y_all = torch.empty_like(x_all)
+        scratch = stack._scratch(m)
+        step = lambda: stack.forward(x_all, y_all, scratch)  # noqa: E731
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for _ in range(args.warmup):
+        if flush is not None:
+            flush.fill_(1)
+        step()
+    torch.cuda.synchronize()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(dev) as clocks:
+        for i in range(args.steps):
+            if flush is not None:
+                flush.fill_(1)
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    step_ms_local = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
+    step_ms = step_ms_local
+    if world > 1:
+        t = torch.tensor([step_ms_local], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        step_ms = float(t.item())
+
+    # Dominant kernel, timed alone: the fused gate/up + SiLU*up kernel of layer 0.
+    w0 = stack.layers[0]
+    dom = dominant_kernel(stack, w0, x_all[0], flush, stream, m)
+
+    # End to end through the public API with host buffers (H2D of the step's inputs, D2H of its outputs).
+    e2e = end_to_end(stack, x_all, m, args, flush, barrier, world, dev)
+
+    pk, pk_kind = peaks()
+    decode = m <= 64
+    if decode:
+        achieved = dom["bytes"] / (dom["ms"] * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": traffic_from_profiles(wl, "gate_up")}
+    else:
+        achieved = dom["flops"] / (dom["ms"] * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": traffic_from_profiles(wl, "gate_up")}
+    roof["peak_source"] = f"of {pk_kind}"
+    roof["kernel"] = dom["name"]
+    roof["kernel_ms"] = round(dom["ms"], 5)
+    roof["algorithmic_per_launch"] = dom["bytes"] if decode else dom["flops"]
+
+    tokens_per_s = m / (step_ms * 1e-3)
+    stack_bytes = L * layer_bytes(h, inter, m)
+    stack_flops = L * layer_flops(h, inter, m)
+    line = {
+        "metric": "ffn_tokens_per_s", "value": round(tokens_per_s, 2), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded W4A16 group-128, N(0,1) bf16)",
+        "config": {"workload": f"{wl['name']}: {wl['model']} x{L} layers, M={m}", "hidden": h, "intermediate": inter,
+                   "layers": L, "m": m, "parallelism": f"tp{world}" if world > 1 else "single",
+                   "l2": "flushed between steps (2x L2 buffer write)" if flush is not None else "weights larger than L2",
+                   "graph": use_graph},
+        "decode_hbm_gbs" if decode else "prefill_tflops":
+            round(stack_bytes / (step_ms * 1e-3) / 1e9, 1) if decode else round(stack_flops / (step_ms * 1e-3) / 1e12, 1),
+        "roofline": roof,
+        "clocks": clocks.summary(),
+        "e2e": e2e,
+        "gpu_launches": stack.kernels_per_step() * args.steps,
+    }
+    if rank == 0 and world == 1:
+        line["cpu_baseline"] = cpu_baseline(wl, m, args.cpu_sample_s)
+    stack.release()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def dominant_kernel(stack, w, x, flush, stream, m, reps=20):
+    import torch
+
+    from heteromega_b200 import _lib
+    from heteromega_b200.torch_ops import ops
+
+    n, stored, h = w.channels(), w.stored_channels(), w.hidden
+    act = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
+
+    def launch():
+        ops.w4a16_gemv(act, x, w.gate_up, h, 2 * n, h, 2 * stored, 0, _lib.HMB_EPI_SWIGLU, int(w.layout), 0)
+
+    launch()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        launch()
+    big = flush if flush is not None else torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=x.device)
+    times = []
+    for _ in range(reps):
+        big.fill_(1)  # keeps the GPU busy while the graph is enqueued, and evicts the weights from L2
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        g.replay()
+        e.record(stream)
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    ms = statistics.median(times)
+    return {"name": "gemv_kernel<swiglu> (gate/up + SiLU*up)" if m <= 64 else "gate/up GEMM + SiLU*up", "ms": ms,
+            "bytes": h * 2 * n * BYTES_PER_WEIGHT + m * h * 2 + m * n * 2, "flops": 2.0 * m * h * 2 * n}
+
+
+def end_to_end(stack, x_all, m, args, flush, barrier, world, dev):
+    import torch
+    import torch.distributed as dist
+
+    x_host = x_all.cpu().pin_memory()
+    y_host = torch.empty_like(x_host).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        stack.forward_host(x_host, y_host)
+    torch.cuda.synchronize()
+    barrier()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        if flush is not None:
+            flush.fill_(1)
+        starts[i].record(stream)
+        stack.forward_host(x_host, y_host)
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    nbytes = x_host.numel() * x_host.element_size()
+    return {"value": round(m / (ms * 1e-3), 2), "unit": "tokens/s", "h2d_bytes_per_step": nbytes,
+            "d2h_bytes_per_step": nbytes, "ms_per_step": round(ms, 5), "api": "FfnStack.forward_host"}
+
+
+def traffic_from_profiles(wl, kernel):
+    """DRAM bytes per launch of the dominant kernel from a committed ncu summary, if one exists."""
+    path = os.path.join(REPO, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            t = json.load(f)
+        return t[f"{wl['name']}_m{wl['m']}"][kernel]
+    except (OSError, KeyError, ValueError):
+        return None
+
+
+# ---- CPU: the reference's own AVX kernel (oracle/_ref), or the oracle port ------------------------------
+
+def cpu_ffn_setup(wl, rows):
+    import numpy as np
+
+    from oracle import oracle as O
+
+    h, n = wl["hidden"], wl["inter"]
+    rng = np.random.default_rng(1000)
+    gate_up = rng.integers(0, 256, (h // 128) * (2 * n // 64) * 4352, dtype=np.uint8)
+    down = rng.integers(0, 256, (n // 128) * (h // 64) * 4352, dtype=np.uint8)
+    for p, k, nn in ((gate_up, h, 2 * n), (down, n, h)):
+        t = p.reshape(-1, 4352)
+        t[:, 4096:4224] = O.bf16_bits(rng.uniform(0.002, 0.02, (t.shape[0], 64))).view(np.uint8).reshape(-1, 128)
+        z = rng.integers(0, 16, (t.shape[0], 8, 8), dtype=np.uint8)
+        t[:, 4224:] = np.concatenate([z, z], 2).reshape(-1, 128)
+    x = O.bf16_bits(np.random.default_rng(7).standard_normal((rows, h)))
+    return O, gate_up, down, x
+
+
+def cpu_layer_runner(wl, rows):
+    """A callable that runs the FFN of one layer for `rows` tokens on the host, and its description."""
+    O, gate_up, down, x = cpu_ffn_setup(wl, rows)
+    h, n = wl["hidden"], wl["inter"]
+    threads = os.cpu_count() or 1
+    if O.ReferenceAVX.available():
+        avx = O.ReferenceAVX()
+
+        def run():
+            for r in range(rows):
+                gu = avx.gemv(x[r], gate_up, h, 2 * n, threads)
+                act = O.silu_mul(gu[None, :], n, 1)[0]
+                avx.gemv(act, down, n, h, threads)
+
+        kind = "reference"
+        what = ("w4a16_gemv_cpu_fused_packed (src/cpu_avx_kernels/w4a16_gemv_avx_packed.cpp, built unchanged, "
+                + ("AVX512-BF16" if avx.avx512 else "scalar branch: host lacks AVX512-BF16") + ")")
+    else:
+        def run():
+            O.ffn(gate_up, down, h, n, n, 1, x)
+
+        kind = "port"
+        what = "C oracle (oracle/w4a16_oracle.c, OpenMP)"
+    return run, kind, what, threads
+
+
+def cpu_baseline(wl, m, budget_s):
+    """Rank-0 CPU baseline on a bounded sample: a few tokens through one layer, scaled to the
+    workload's tokens/s (per token, the stack takes `layers` times one layer)."""
+    rows = 1 if m <= 64 else 4
+    run, kind, what, threads = cpu_layer_runner(wl, rows)
+    run()  # warm-up
+    t0 = time.perf_counter()
+    run()
+    one = time.perf_counter() - t0
+    reps = max(3, min(200, int(budget_s / max(one, 1e-6))))
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    per_layer_token = statistics.median(times) / rows
+    tokens_per_s = 1.0 / (per_layer_token * wl["layers"])
+    return {"value": round(tokens_per_s, 3), "unit": "tokens/s", "cores": threads, "kind": kind,
+            "sample": f"{reps} x {rows} token(s) through one {wl['hidden']}x{wl['inter']} layer (median), "
+                      f"scaled to {wl['layers']} layer(s); {what}; {cpu_model()}"}
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown CPU"
+
+
+def run_reference(args):
+    """The reference arm: the reference's CPU implementation of the path, timed on the host cores, on
+    this arm's config and metric. Rank 0 only; other ranks exit without work."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    wl = workload(args)
+    m = wl["m"]
+    rows = 1 if m <= 64 else 4
+    run, kind, what, threads = cpu_layer_runner(wl, rows)
+    layers_sampled = 1
+    for _ in range(args.warmup):
+        run()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    per_token_stack = statistics.median(times) / rows * wl["layers"] / layers_sampled
+    value = 1.0 / per_token_stack
+    line = {
+        "metric": "ffn_tokens_per_s", "value": round(value, 3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_token_stack * m * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded W4A16 group-128, N(0,1) bf16)", "impl": "reference",
+        "config": {"workload": f"{wl['name']}: {wl['model']} x{wl['layers']} layers, M={m}", "hidden": wl["hidden"],
+                   "intermediate": wl["inter"], "layers": wl["layers"], "m": m, "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": kind,
+                         "sample": f"each step: {rows} token(s) through one layer, scaled to M={m} x {wl['layers']} "
+                                   f"layer(s); {what}; {cpu_model()}"},
+        "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_hmb(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,161 @@
+"""PyTorch custom operators ``torch.ops.heteromega.*`` over the C ABI of libhmb.so.
+
+Each operator checks its tensors the way the reference's TORCH_CHECKs do, then calls the
+C entry point on the current CUDA stream of the tensors' device. The operators only
+enqueue work; they never synchronize. Split-K workspaces are cached per (device, stream),
+like the per-stream scratch of the reference (kernels/gpu/src/gemm_w4a16.cu:364-376).
+"""
+import threading
+
+import torch
+
+from . import _lib
+from ._lib import check, lib
+
+_ws_lock = threading.Lock()
+_workspaces = {}
+
+
+def _stream(t):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t):
+    return t.data_ptr() if t is not None else None
+
+
+def workspace(device, nbytes):
+    """A zero-filled uint8 buffer of at least nbytes for the current stream of `device`.
+    Calls on one stream reuse it; the kernels leave its counter words zero."""
+    stream = torch.cuda.current_stream(device)
+    key = (device.index, stream.cuda_stream)
+    with _ws_lock:
+        buf = _workspaces.get(key)
+        if buf is None or buf.numel() < nbytes:
+            size = max(nbytes, 1 << 20)
+            if buf is not None:
+                size = max(size, 2 * buf.numel())
+            buf = torch.zeros(size, dtype=torch.uint8, device=device)
+            _workspaces[key] = buf
+        return buf
+
+
+def _dtype_code(t):
+    if t.dtype == torch.bfloat16:
+        return _lib.HMB_BF16
+    if t.dtype == torch.float16:
+        return _lib.HMB_FP16
+    if t.dtype == torch.float32:
+        return _lib.HMB_FP32
+    raise TypeError(f"unsupported dtype {t.dtype}")
+
+
+def _rows(t):
+    return t.shape[0] if t.dim() == 2 else 1
+
+
+def _ld(t):
+    return t.stride(0) if t.dim() == 2 else t.shape[-1]
+
+
+def _check_cuda(*ts):
+    dev = ts[0].device
+    for t in ts:
+        if not t.is_cuda or t.device != dev:
+            raise ValueError("heteromega: all tensors must be CUDA tensors on one device")
+
+
+_defs = torch.library.Library("heteromega", "DEF")
+_defs.define("w4a16_gemv(Tensor(a!) out, Tensor x, Tensor packed, int k, int n, int packed_k, int packed_n, "
+             "int start_col, int epilogue, int layout, int split_k) -> ()")
+_defs.define("w4a16_dequant(Tensor(a!) out, Tensor packed, int k, int n, int packed_k, int packed_n) -> ()")
+_defs.define("silu_mul(Tensor gate_up, Tensor(a!) act, int layout) -> ()")
+_defs.define("residual_add2(Tensor(a!) x, Tensor y_g, Tensor y_n) -> ()")
+_defs.define("gather_tiles(Tensor(a!) dst, Tensor src0, Tensor src1, Tensor idx) -> ()")
+_defs.define("pack_w4a16_device(Tensor(a!) out, Tensor q, Tensor scales, Tensor zeros, Tensor(b!) bad) -> ()")
+
+
+def _w4a16_gemv(out, x, packed, k, n, packed_k, packed_n, start_col, epilogue, layout, split_k):
+    _check_cuda(out, x, packed)
+    if x.dim() not in (1, 2) or out.dim() not in (1, 2) or x.stride(-1) != 1 or out.stride(-1) != 1:
+        raise ValueError("w4a16_gemv: x and out must be [M, K] / [M, N] with contiguous rows")
+    m = _rows(x)
+    if _rows(out) != m:
+        raise ValueError("w4a16_gemv: x and out must have the same number of rows")
+    if packed.dtype != torch.uint8 or not packed.is_contiguous():
+        raise ValueError("w4a16_gemv: packed must be contiguous uint8")
+    if packed.numel() != lib().hmb_packed_bytes(packed_k, packed_n):
+        raise ValueError(f"w4a16_gemv: packed has {packed.numel()} bytes, not those of [{packed_k}, {packed_n}]")
+    ws_bytes = lib().hmb_w4a16_gemv_workspace(m, k, n, epilogue, split_k)
+    ws = workspace(x.device, ws_bytes)
+    check(lib().hmb_w4a16_gemv(packed.data_ptr(), packed_k, packed_n, x.data_ptr(), _ld(x), _dtype_code(x), out.data_ptr(),
+                               _ld(out), _dtype_code(out), m, k, n, start_col, epilogue, layout, split_k, ws.data_ptr(),
+                               ws.numel(), _stream(x)), "w4a16_gemv")
+
+
+def _w4a16_dequant(out, packed, k, n, packed_k, packed_n):
+    _check_cuda(out, packed)
+    if out.dtype != torch.float32 or out.dim() != 2 or out.stride(1) != 1 or out.shape[0] != k or out.shape[1] != n:
+        raise ValueError("w4a16_dequant: out must be fp32 [k, n] with contiguous rows")
+    if packed.numel() != lib().hmb_packed_bytes(packed_k, packed_n):
+        raise ValueError("w4a16_dequant: packed size does not match")
+    check(lib().hmb_w4a16_dequant(packed.data_ptr(), packed_k, packed_n, k, n, out.data_ptr(), out.stride(0), _stream(out)),
+          "w4a16_dequant")
+
+
+def _silu_mul(gate_up, act, layout):
+    _check_cuda(gate_up, act)
+    if gate_up.dim() != 2 or act.dim() != 2:
+        raise ValueError("silu_mul: expected 2-D tensors")
+    if gate_up.dtype != torch.bfloat16 or act.dtype != torch.bfloat16:
+        raise ValueError("silu_mul: expected bf16")
+    rows, n = act.shape
+    if gate_up.shape[0] != rows or gate_up.shape[1] != 2 * n:
+        raise ValueError("silu_mul: gate_up must be [M, 2n] and act [M, n]")
+    if gate_up.stride(1) != 1 or act.stride(1) != 1:
+        raise ValueError("silu_mul: last dimension must be contiguous")
+    check(lib().hmb_silu_mul(gate_up.data_ptr(), gate_up.stride(0), act.data_ptr(), act.stride(0), rows, n, layout,
+                             _stream(act)), "silu_mul")
+
+
+def _residual_add2(x, y_g, y_n):
+    _check_cuda(x, y_g, y_n)
+    if x.dim() != 2 or x.dtype != torch.bfloat16:
+        raise ValueError("residual_add2: x must be bf16 [M, H]")
+    for name, t in (("y_g", y_g), ("y_n", y_n)):
+        if t.dim() != 2 or tuple(t.shape) != tuple(x.shape):
+            raise ValueError(f"residual_add2: {name} must match x")
+        if t.dtype not in (torch.bfloat16, torch.float32):
+            raise ValueError(f"residual_add2: {name} must be bf16 or fp32")
+        if t.stride(1) != 1:
+            raise ValueError(f"residual_add2: {name} needs a contiguous last dim")
+    check(lib().hmb_residual_add2(x.data_ptr(), x.stride(0), y_g.data_ptr(), y_g.stride(0), _dtype_code(y_g), y_n.data_ptr(),
+                                  y_n.stride(0), _dtype_code(y_n), x.shape[0], x.shape[1], _stream(x)), "residual_add2")
+
+
+def _gather_tiles(dst, src0, src1, idx):
+    _check_cuda(dst, src0, src1, idx)
+    if idx.dtype != torch.int64 or not idx.is_contiguous():
+        raise ValueError("gather_tiles: idx must be contiguous int64")
+    if dst.numel() != idx.numel() * _lib.TILE_BYTES:
+        raise ValueError("gather_tiles: dst must hold one tile per index")
+    check(lib().hmb_gather_tiles(src0.data_ptr(), src0.numel() // _lib.TILE_BYTES, src1.data_ptr(), idx.data_ptr(),
+                                 idx.numel(), dst.data_ptr(), _stream(dst)), "gather_tiles")
+
+
+def _pack_w4a16_device(out, q, scales, zeros, bad):
+    _check_cuda(out, q, scales, zeros, bad)
+    k, n = q.shape
+    check(lib().hmb_pack_w4a16_device(q.data_ptr(), scales.data_ptr(), zeros.data_ptr(), k, n, out.data_ptr(),
+                                      bad.data_ptr(), _stream(out)), "pack_w4a16_device")
+
+
+_impls = torch.library.Library("heteromega", "IMPL", "CUDA")
+_impls.impl("w4a16_gemv", _w4a16_gemv)
+_impls.impl("w4a16_dequant", _w4a16_dequant)
+_impls.impl("silu_mul", _silu_mul)
+_impls.impl("residual_add2", _residual_add2)
+_impls.impl("gather_tiles", _gather_tiles)
+_impls.impl("pack_w4a16_device", _pack_w4a16_device)
+
+ops = torch.ops.heteromega

@@ -1,0 +1,141 @@
+/*
+ * heteromega-b200: C ABI of the B200-native W4A16 SwiGLU FFN engine (libhmb.so).
+ *
+ * The entry points replace the kernel interfaces of glassescrab/HeteroMega's FFN hot
+ * path; each declaration names the reference interface it stands in for
+ * (file:line inside that project). Conventions, shared by every entry point:
+ *
+ *   - Plain pointers and sizes only. Device entry points take device pointers and
+ *     enqueue on `stream` (0 = the legacy default stream); they never synchronize and
+ *     never allocate. Host entry points (hmb_pack_*, hmb_slice_*) run on the CPU.
+ *   - Return 0 (HMB_OK) or a negative hmb_status. Nothing calls exit() or throws.
+ *     After HMB_ERR_CUDA, hmb_last_cuda_error() gives the cudaError_t of the call.
+ *   - Packed weights use the reference's tile layout unchanged: 128 (K) x 64 (N)
+ *     tiles of 4352 bytes (4096 nibble bytes, 64 bf16 scales, 64 zeros stored
+ *     twice), ordered by tile column modulo 8, tile column, tile row
+ *     (kernels/gpu/include/heteromega/gpu_ffn.hpp:18-20, kernels/gpu/src/pack_w4a16.cpp:30-61).
+ *     A packed [packed_k, packed_n] matrix can be used through its leading [k, n] block.
+ *   - Activations are row-major bf16 (or fp16 where x_dtype allows it) with a row stride
+ *     in elements. Alignment: packed 16 bytes; x, y 16 bytes; strides multiples of 8.
+ *   - Entry points that take `workspace` use it for split-K partial sums. It is owned by
+ *     the caller, must be zero-filled once before its first use, and is left with its
+ *     counter words zero after every call. Calls that run at the same time on different
+ *     streams need different workspaces. hmb_*_workspace() gives the size.
+ */
+#ifndef HMB_H
+#define HMB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *hmb_stream_t; /* a cudaStream_t */
+
+enum { HMB_TILE_K = 128, HMB_TILE_N = 64, HMB_TILE_BYTES = 4352 };
+
+typedef enum hmb_status {
+    HMB_OK = 0,
+    HMB_ERR_ARG = -1,         /* null pointer, bad size or bad enum value */
+    HMB_ERR_ALIGN = -2,       /* pointer or stride alignment */
+    HMB_ERR_VALUE = -3,       /* a weight or zero point outside 0..15 */
+    HMB_ERR_WORKSPACE = -4,   /* workspace missing or too small */
+    HMB_ERR_UNSUPPORTED = -5, /* a shape this build does not handle */
+    HMB_ERR_CUDA = -6,        /* a CUDA call failed; see hmb_last_cuda_error() */
+    HMB_ERR_TIMEOUT = -7      /* a bounded device-side wait gave up */
+} hmb_status;
+
+typedef enum hmb_dtype { HMB_BF16 = 0, HMB_FP16 = 1, HMB_FP32 = 2 } hmb_dtype;
+
+/* Column order of a packed gate_up matrix of n channels (gpu_ffn.hpp:50-54). */
+typedef enum hmb_gate_up_layout {
+    HMB_GATE_UP_BLOCKED = 0,    /* [gate 0..n | up 0..n] */
+    HMB_GATE_UP_INTERLEAVED = 1 /* per 64 channels: 64 gate columns, then 64 up columns */
+} hmb_gate_up_layout;
+
+typedef enum hmb_epilogue {
+    HMB_EPI_STORE = 0, /* y = x @ W */
+    HMB_EPI_SWIGLU = 1 /* W is gate_up [k, 2c] in `layout` order; y[:, j] = SiLU(gate_j) * up_j, c columns */
+} hmb_epilogue;
+
+const char *hmb_status_string(int status);
+int hmb_version(void);
+int hmb_last_cuda_error(void);
+
+/* ---- packed layout, host side ------------------------------------------------------------- */
+
+/* Bytes of a packed [k, n] matrix: (k/128) * (n/64) * 4352. -1 if k % 128 or n % 64. */
+int64_t hmb_packed_bytes(int64_t k, int64_t n);
+
+/* Position of tile (column c, row r) in a packed tiles_k x tiles_n matrix.
+ * Replaces heteromega::packed_tile_index (kernels/gpu/src/pack_w4a16.cpp:100-107). */
+int64_t hmb_packed_tile_index(int64_t c, int64_t r, int64_t tiles_k, int64_t tiles_n);
+
+/* Packs q [k, n] (0..15), scales [k/128, n] (bf16 bits) and zeros [k/128, n] (0..15) into `out`
+ * (hmb_packed_bytes(k, n) bytes). HMB_ERR_VALUE if a value exceeds 15.
+ * Replaces heteromega::pack_w4a16 (gpu_ffn.hpp:34; pack_w4a16.cpp:9-66) and HeteroMosaic's
+ * _pack_weights_packed without padding (py/unified_llm_w4a16/llama3_8b_w4a16_model.py:546-656). */
+int hmb_pack_w4a16(const uint8_t *q, const uint16_t *scales_bf16, const uint8_t *zeros, int64_t k, int64_t n, uint8_t *out);
+
+/* Tile counts of the channel slice [begin, end) of an FFN layer with `hidden` rows and `inter`
+ * channels: gate_up [hidden, 2(end-begin)] and down [end-begin, hidden]. */
+int hmb_slice_tile_counts(int64_t hidden, int64_t inter, int64_t begin, int64_t end, int64_t *gate_up_tiles,
+                          int64_t *down_tiles);
+
+/* For each tile of the slice, the source tile it copies: gate_up_src indexes the concatenation
+ * [gate tiles | up tiles] of the packed gate [hidden, inter] and up [hidden, inter]; down_src
+ * indexes the packed down [inter, hidden]. begin and end are multiples of 128.
+ * Replaces the index computation of heteromega::slice_packed_ffn (pack_w4a16.cpp:109-165). */
+int hmb_slice_tile_map(int64_t hidden, int64_t inter, int64_t begin, int64_t end, int layout, int64_t *gate_up_src,
+                       int64_t *down_src);
+
+/* ---- device ------------------------------------------------------------------------------- */
+
+/* dst tile i = (idx[i] < src0_tiles ? src0 tile idx[i] : src1 tile idx[i] - src0_tiles).
+ * idx is a device array of `count` int64. The tile gather of slice_packed_ffn
+ * (pack_w4a16.cpp:124-128, 143, 158) on the device. src1 may be null when every idx < src0_tiles. */
+int hmb_gather_tiles(const uint8_t *src0, int64_t src0_tiles, const uint8_t *src1, const int64_t *idx, int64_t count,
+                     uint8_t *dst, hmb_stream_t stream);
+
+/* The packer of hmb_pack_w4a16 on device pointers. Values above 15 are masked to 4 bits and make
+ * the kernel set *bad_flag (a device int, may be null) to 1. */
+int hmb_pack_w4a16_device(const uint8_t *q, const uint16_t *scales_bf16, const uint8_t *zeros, int64_t k, int64_t n,
+                          uint8_t *out, int *bad_flag, hmb_stream_t stream);
+
+/* out[r][c] (fp32, row stride ldo) = (q - zero) * scale for the leading [k, n] block. Exact.
+ * The dequantization the reference's kernels and oracle apply
+ * (src/cpu_avx_kernels/w4a16_gemv_avx_packed.cpp:255-281; gpu_ffn_test dequant, kernels/gpu/tests/test_gpu_ffn.cpp:75-80). */
+int hmb_w4a16_dequant(const uint8_t *packed, int64_t packed_k, int64_t packed_n, int64_t k, int64_t n, float *out, int64_t ldo,
+                      hmb_stream_t stream);
+
+/* Decode GEMV / skinny GEMM on CUDA-core-free tensor-core fragments (mma.sync), for m <= 16 per
+ * launch (larger m is processed in chunks of 16 rows):
+ *   HMB_EPI_STORE:  y[m, n] = x[m, k] @ W[:k, start_col : start_col + n]
+ *   HMB_EPI_SWIGLU: W[:k, start_col : start_col + n] is gate_up of n/2 channels in `layout` order and
+ *                   y[m, n/2] = bf16(SiLU(g) * u) with g, u the bf16-rounded gate and up sums.
+ * x_dtype: HMB_BF16 or HMB_FP16; y_dtype: x_dtype or HMB_FP32 (unrounded sums, HMB_EPI_STORE only).
+ * split_k <= 0 picks the split from the shape; a split > 1 needs the workspace.
+ * Replaces hipkernels::w4a16_gemv_fused_packed (include/hipkernels/w4a16_gemm_packed.hpp:52-53) and
+ * heteromega::gemv_w4a16 (gpu_ffn.hpp:98-99), plus the SiLU*up that the model runs after gate/up
+ * (kernels/gpu/src/silu_mul.cu; unified_llm_w4a16.cpp:2881-2883). */
+int hmb_w4a16_gemv(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const void *x, int64_t ldx, int x_dtype, void *y,
+                   int64_t ldy, int y_dtype, int64_t m, int64_t k, int64_t n, int64_t start_col, int epilogue, int layout,
+                   int split_k, void *workspace, size_t workspace_bytes, hmb_stream_t stream);
+size_t hmb_w4a16_gemv_workspace(int64_t m, int64_t k, int64_t n, int epilogue, int split_k);
+
+/* act[m, n] = bf16(SiLU(g) * u), fp32 math, one rounding; gate_up [m, 2n] in `layout` order.
+ * Replaces heteromega::silu_mul (gpu_ffn.hpp:92-93; silu_mul.cu:34-57). */
+int hmb_silu_mul(const void *gate_up, int64_t ld_in, void *act, int64_t ld_out, int64_t m, int64_t n, int layout,
+                 hmb_stream_t stream);
+
+/* x[m, cols] += y_g + y_n (partials first, fp32 math, one bf16 rounding); y_g, y_n bf16 or fp32.
+ * Replaces heteromega::residual_add2 (gpu_ffn.hpp:159; residual_add.cu:55-73). */
+int hmb_residual_add2(void *x, int64_t ldx, const void *y_g, int64_t ldg, int g_dtype, const void *y_n, int64_t ldn,
+                      int n_dtype, int64_t m, int64_t cols, hmb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HMB_H */
