@@ -1,149 +1,188 @@
-// W4A16 decode GEMV / skinny GEMM (m <= 16 rows) on the packed tile layout.
+// W4A16 decode GEMV / skinny GEMM (m <= 16 rows per launch) on the packed tile layout.
 //
 // What it computes is the reference's GEMV definition (src/cpu_avx_kernels/w4a16_gemv_avx_packed.cpp:83-289,
 // kernels/gpu/src/gemv_w4a16.cu:27-28): for each 128-row tile and column,
 //     s * (sum_r q_r * x_r - z * sum_r x_r)     in fp32,
 // summed over the tiles of a column, then rounded once. How it computes it is B200-specific:
 //
-//   * One warp consumes one whole 4352-byte tile per step: eight 16-byte streaming loads per lane,
-//     512 contiguous bytes per warp load, no shared memory and no __syncthreads in the K loop.
+//   * Work is the stream of packed tiles. The tiles of a "column set" (one tile column, or the gate
+//     and up tile columns of 64 channels for the SwiGLU epilogue) form consecutive items, and the
+//     whole item range is cut into equal contiguous chunks, one per warp of a grid of one CTA per
+//     SM. Every warp streams its chunk through a private 5-stage ring of 16-byte cp.async copies
+//     in shared memory (4 tiles in flight per warp, ~128 KB per SM), so a small matrix is requested
+//     from HBM at once and a large one keeps the memory system full.
 //   * The weights go through the tensor cores as exact integers. A nibble q becomes the bf16
 //     (fp16) number 128 + q (1024 + q) by OR-ing it into the mantissa of 0x4300 (0x6400), so one
-//     PRMT and two LOP3 turn 4 bytes into 4 MMA operand registers. The MMA multiplies them with
-//     x and accumulates in fp32; an extra MMA with an all-ones operand yields sum_r x_r in the
-//     same fragment positions. Per tile and column:
-//         s * (acc - (C + z) * sum_x) = s * (sum q*x - z * sum x)        (C = 128 or 1024).
-//   * The MMA is m16n8k16 with the weights on the M side ("swap AB"): 16 output columns x 8 rows
-//     of x. The packed layout stores, per K row, 8 consecutive columns in one 32-bit word. A lane
-//     with group g = lane/4 and t = lane%4 takes column group g and K rows 4t..4t+3 of each
-//     16-row chunk; K inside a chunk is permuted so that these 4 rows form the lane's operand
-//     pairs, and x is read with the same permutation, so the dot products are unchanged. Of the
-//     8 columns of its group, the lane feeds columns 2b and 2b+1 to MMA block b (b = 0..3).
-//   * Split-K over CTAs writes fp32 partial sums to the workspace; the last CTA of a column set
-//     (an atomic counter) adds them in split order, so results do not depend on timing.
-//   * The SwiGLU epilogue pairs the gate and up tile columns of 64 channels in one CTA and
-//     writes bf16(SiLU(g) * u) from the bf16-rounded g and u, so gate/up never reach HBM.
+//     PRMT and two LOP3 turn 4 bytes into MMA operand registers. The MMA multiplies them with x and
+//     accumulates in fp32; an extra MMA with an all-ones operand yields sum_r x_r in the same
+//     fragment positions. Per tile and column: s * (acc - (C + z) * sum_x) = s * (sum q*x - z*sum x).
+//   * The MMA is m16n8k16 with the weights on the M side ("swap AB"): 16 output columns x 8 rows of
+//     x. The packed layout stores, per K row, 8 consecutive columns in one 32-bit word. A lane with
+//     g = lane/4, t = lane%4 takes column group g and K rows 4t..4t+3 of each 16-row chunk; K inside
+//     a chunk is permuted so that these rows form the lane's operand pairs, and x is read with the
+//     same permutation, so the dot products are unchanged. Column 2b/2b+1 of the group feed MMA
+//     block b.
+//   * A column set that lies inside one warp's chunk is finished from that warp's registers. One
+//     that crosses chunks is finished by the last warp to contribute (an atomic counter per column
+//     set): it adds the fp32 partials of all contributors in chunk order, so results do not depend
+//     on timing.
+//   * The SwiGLU epilogue writes bf16(SiLU(g) * u) from the bf16-rounded gate and up sums of the
+//     same lane, so gate/up never reach HBM.
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
 namespace hmb {
 namespace {
 
-constexpr int kWarps = 4;
-constexpr int kThreads = kWarps * 32;
+constexpr int kSmemBudget = 224 * 1024;
+constexpr int kXRowBytes = 288;  // 256 bytes of x per row and tile, padded so 4 rows hit distinct banks
+
+// Per-warp ring stage: [8 x 512 weight bytes, lane-major][128 scale bytes][128 zero bytes][m x 288 x bytes].
+__host__ __device__ constexpr int stage_bytes(int m) { return 4352 + kXRowBytes * m; }
 
 struct GemvArgs {
     const uint8_t *packed;
     const uint16_t *x;
     void *y;
-    float *partial;   // [splits][m][n] fp32, n = computed columns
-    int *counters;    // [column sets]
+    float *partial;  // contributor slots of column sets that cross warp chunks
+    int *counters;   // [column sets]
     int64_t ldx, ldy;
     int tiles_k_total, tiles_n_total;  // the whole packed matrix
     int col_tile0;                     // first tile column used
     int k_tiles;                       // tile rows used
-    int n_tiles;                       // tile columns used
-    int m;
-    int splits, tiles_per_split;
+    int colsets;
     int col_stride;  // tile columns between slot 0 and slot 1 of a column set (pairs only)
+    int m;
     int y_f32;
+    int items;  // colsets * NCOL * k_tiles
+    int warps;  // warps that share the items
 };
 
 template <bool F16>
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                          uint32_t b1) {
     if constexpr (F16) {
-        asm volatile(
-            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
             : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
             : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
     } else {
-        asm volatile(
-            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
             : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
             : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
     }
 }
 
-struct TileRegs {
-    uint4 w[8];  // chunk j: K rows 16j + 4t .. +3 of column group g
-    uint4 s;     // 8 bf16 scales of column group g
-    uint2 z;     // 8 zeros of column group g
-};
+__device__ __forceinline__ void cp_async16(uint32_t smem, const void *gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// Shared-memory loads as plain C++ accesses: ordered after cp.async.wait_group (its "memory" clobber)
+// and otherwise free for the compiler to schedule early. a is an offset from the dynamic smem base.
+extern __shared__ __align__(128) uint8_t g_smem[];
+__device__ __forceinline__ uint4 lds128(uint32_t a) { return *reinterpret_cast<const uint4 *>(g_smem + a); }
+__device__ __forceinline__ uint2 lds64(uint32_t a) { return *reinterpret_cast<const uint2 *>(g_smem + a); }
 
-__device__ __forceinline__ void load_tile(TileRegs &r, const uint8_t *tile, int lane_off, int g) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) r.w[j] = ld_stream16(tile + 512 * j + lane_off);
-    r.s = ld_stream16(tile + 4096 + 16 * g);
-    r.z = ld_stream8(tile + 4224 + 16 * g);
+// (a & b) | c in one LOP3 (0xEA is the truth table of that expression).
+__device__ __forceinline__ uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
 }
 
-// Accumulates one tile into tot. MT token blocks of 8 rows of x.
+
+
+template <bool F16>
+__device__ __forceinline__ void mma16816_zc(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                            uint32_t b1) {
+    const float z = 0.0f;
+    if constexpr (F16) {
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+            : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
+    } else {
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+            : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
+    }
+}
+
+// Accumulates one staged tile into acc: acc += s * (sum (C+q) x - (C+z) sum x) for the lane's fragment.
+// xrow[mt]: shared address of this lane's x row for token block mt (rows past m repeat row m-1; their
+// results are never stored).
 template <int MT, bool F16>
-__device__ __forceinline__ void tile_mma(const TileRegs &r, const uint16_t *__restrict__ x, int64_t ldx, int m, int64_t krow0,
-                                         int g, int t, float (&tot)[MT][4][4]) {
+__device__ __forceinline__ void tile_mma(uint32_t st, uint32_t wlane, const uint32_t (&xrow)[MT], int g,
+                                         float (&acc)[MT][4][4]) {
     constexpr uint32_t kMagic = F16 ? 0x64006400u : 0x43004300u;
     constexpr uint32_t kOnes = F16 ? 0x3C003C00u : 0x3F803F80u;
     constexpr float kOffset = F16 ? 1024.0f : 128.0f;
     constexpr uint32_t kMask = 0x000F000Fu;
-    float acc[MT][4][4];
+    constexpr uint32_t kMaskHi = 0x00F000F0u;
+    float d[MT][4][4];
     float sx[MT][4];
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            sx[mt][i] = 0.0f;
-#pragma unroll
-            for (int b = 0; b < 4; ++b) acc[mt][b][i] = 0.0f;
-        }
-    }
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         uint32_t bx[MT][2];
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
-            const int tok = mt * 8 + g;
-            if (tok < m) {
-                const uint2 v = *reinterpret_cast<const uint2 *>(x + tok * ldx + krow0 + 16 * j + 4 * t);
-                bx[mt][0] = v.x;
-                bx[mt][1] = v.y;
+            const uint2 v = lds64(st + xrow[mt] + 32 * j);
+            bx[mt][0] = v.x;
+            bx[mt][1] = v.y;
+            if (j == 0) {
+                mma16816_zc<F16>(sx[mt], kOnes, kOnes, kOnes, kOnes, bx[mt][0], bx[mt][1]);
             } else {
-                bx[mt][0] = 0u;
-                bx[mt][1] = 0u;
+                mma16816<F16>(sx[mt], kOnes, kOnes, kOnes, kOnes, bx[mt][0], bx[mt][1]);
             }
-            mma16816<F16>(sx[mt], kOnes, kOnes, kOnes, kOnes, bx[mt][0], bx[mt][1]);
         }
-        const uint4 w = r.w[j];
+        const uint4 w = lds128(st + wlane + 512 * j);
 #pragma unroll
         for (int b = 0; b < 4; ++b) {
             // Byte b of rows (4t, 4t+1) and of rows (4t+2, 4t+3), side by side in 16-bit halves.
             const uint32_t sel = static_cast<uint32_t>(b | (b << 4) | ((4 + b) << 8) | ((4 + b) << 12));
             const uint32_t p = prmt(w.x, w.y, sel);
             const uint32_t q = prmt(w.z, w.w, sel);
-            const uint32_t a0 = (p & kMask) | kMagic;         // column 2b, rows 4t, 4t+1
-            const uint32_t a1 = ((p >> 4) & kMask) | kMagic;  // column 2b+1
-            const uint32_t a2 = (q & kMask) | kMagic;         // column 2b, rows 4t+2, 4t+3
-            const uint32_t a3 = ((q >> 4) & kMask) | kMagic;  // column 2b+1
+            const uint32_t a0 = and_or(p, kMask, kMagic);  // column 2b, rows 4t, 4t+1
+            const uint32_t a2 = and_or(q, kMask, kMagic);  // column 2b, rows 4t+2, 4t+3
+            // Column 2b+1 (high nibbles). fp16 keeps them in place: 1024 + 16 q is exact in its 10-bit
+            // mantissa, and the fold divides by 16. bf16 has 7 mantissa bits, so the nibble moves down.
+            const uint32_t a1 = F16 ? and_or(p, kMaskHi, kMagic) : and_or(p >> 4, kMask, kMagic);
+            const uint32_t a3 = F16 ? and_or(q, kMaskHi, kMagic) : and_or(q >> 4, kMask, kMagic);
 #pragma unroll
-            for (int mt = 0; mt < MT; ++mt) mma16816<F16>(acc[mt][b], a0, a1, a2, a3, bx[mt][0], bx[mt][1]);
+            for (int mt = 0; mt < MT; ++mt) {
+                if (j == 0) {
+                    mma16816_zc<F16>(d[mt][b], a0, a1, a2, a3, bx[mt][0], bx[mt][1]);
+                } else {
+                    mma16816<F16>(d[mt][b], a0, a1, a2, a3, bx[mt][0], bx[mt][1]);
+                }
+            }
         }
     }
-    const uint32_t sw[4] = {r.s.x, r.s.y, r.s.z, r.s.w};
-    const uint32_t zw[2] = {r.z.x, r.z.y};
+    const uint4 sv = lds128(st + 4096 + 16 * g);
+    const uint2 zv = lds64(st + 4224 + 16 * g);
+    const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
+    const uint32_t zw[2] = {zv.x, zv.y};
+    // High-nibble columns of the fp16 path carry 1024 + 16 q: scale 1/16, offset 1024 + 16 z.
+    constexpr float kHiScale = F16 ? 0.0625f : 1.0f;
+    constexpr float kHiZ = F16 ? 16.0f : 1.0f;
 #pragma unroll
     for (int b = 0; b < 4; ++b) {
         const float s_lo = bf16_to_f32(sw[b] & 0xFFFFu);
-        const float s_hi = bf16hi_to_f32(sw[b]);
-        const uint32_t zz = zw[b >> 1] >> (16 * (b & 1));
-        const float zc_lo = kOffset + static_cast<float>(zz & 0xFFu);
-        const float zc_hi = kOffset + static_cast<float>((zz >> 8) & 0xFFu);
+        const float s_hi = bf16hi_to_f32(sw[b]) * kHiScale;
+        // 2^23 + z as float bits: zero byte 2b (2b+1) of the group under an exponent byte 0x4B.
+        const uint32_t zsel_lo = static_cast<uint32_t>(((2 * b) & 3) | 0x7440), zsel_hi = zsel_lo + 1;
+        const float zc_lo = __uint_as_float(prmt(zw[b >> 1], 0x4B000000u, zsel_lo)) - (8388608.0f - kOffset);
+        const float zc_hi = fmaf(__uint_as_float(prmt(zw[b >> 1], 0x4B000000u, zsel_hi)) - 8388608.0f, kHiZ, kOffset);
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
-            tot[mt][b][0] = fmaf(s_lo, fmaf(-zc_lo, sx[mt][0], acc[mt][b][0]), tot[mt][b][0]);
-            tot[mt][b][1] = fmaf(s_lo, fmaf(-zc_lo, sx[mt][1], acc[mt][b][1]), tot[mt][b][1]);
-            tot[mt][b][2] = fmaf(s_hi, fmaf(-zc_hi, sx[mt][2], acc[mt][b][2]), tot[mt][b][2]);
-            tot[mt][b][3] = fmaf(s_hi, fmaf(-zc_hi, sx[mt][3], acc[mt][b][3]), tot[mt][b][3]);
+            acc[mt][b][0] = fmaf(s_lo, fmaf(-zc_lo, sx[mt][0], d[mt][b][0]), acc[mt][b][0]);
+            acc[mt][b][1] = fmaf(s_lo, fmaf(-zc_lo, sx[mt][1], d[mt][b][1]), acc[mt][b][1]);
+            acc[mt][b][2] = fmaf(s_hi, fmaf(-zc_hi, sx[mt][2], d[mt][b][2]), acc[mt][b][2]);
+            acc[mt][b][3] = fmaf(s_hi, fmaf(-zc_hi, sx[mt][3], d[mt][b][3]), acc[mt][b][3]);
         }
     }
 }
@@ -154,160 +193,270 @@ __device__ __forceinline__ float silu_mul_rounded(float g, float u) {
     return gr / (1.0f + __expf(-gr)) * ur;
 }
 
-// Grid: (column sets, splits). A column set is 1 tile column, or 2 (gate and up of 64 channels).
-template <int NCOL, int MT, bool F16, int EPI>
-__global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvArgs a) {
-    __shared__ float red[kWarps][NCOL][MT * 8][kTileN];
-    __shared__ int s_last;
+// Warp chunk that holds item x: the last gw with floor(gw * items / warps) <= x.
+__device__ __forceinline__ int chunk_of(int x, int items, int warps) {
+    return static_cast<int>(((static_cast<int64_t>(x) + 1) * warps + items - 1) / items - 1);
+}
 
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g = lane >> 2, t = lane & 3;
-    const int lane_off = 256 * (t >> 1) + 32 * g + 16 * (t & 1);
-    const int cs = blockIdx.x;
-    const int base = (NCOL == 2 && a.col_stride == 1) ? 2 * cs : cs;
-    const int kb = blockIdx.y * a.tiles_per_split;
-    const int nk = min(kb + a.tiles_per_split, a.k_tiles) - kb;
-    const int items = NCOL * nk;
-
-    for (int i = threadIdx.x; i < kWarps * NCOL * MT * 8 * kTileN; i += kThreads) (&red[0][0][0][0])[i] = 0.0f;
-    __syncthreads();
-
-    int64_t col_base[NCOL];
+// Writes the finished sums of column set j from one lane's fragment (tok 2t + (i&1), column 8g + 2b + (i>>1)).
+// v0 holds slot 0 (gate, or the only column), v1 slot 1 (up).
+template <int MT, bool F16, int EPI>
+__device__ __forceinline__ void epilogue(const GemvArgs &a, int j, int g, int t, const float (&v0)[MT][4][4],
+                                         const float (&v1)[MT][4][4]) {
 #pragma unroll
-    for (int s = 0; s < NCOL; ++s) {
-        col_base[s] = tile_index(a.col_tile0 + base + s * a.col_stride, 0, a.tiles_k_total, a.tiles_n_total);
+    for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int tok = mt * 8 + 2 * t + h;
+            if (tok >= a.m) continue;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const int c = 8 * g + 2 * b;  // columns c and c + 1 of the tile
+                if constexpr (EPI == HMB_EPI_SWIGLU) {
+                    const float lo = silu_mul_rounded<F16>(v0[mt][b][h], v1[mt][b][h]);
+                    const float hi = silu_mul_rounded<F16>(v0[mt][b][2 + h], v1[mt][b][2 + h]);
+                    uint16_t *y = static_cast<uint16_t *>(a.y) + tok * a.ldy + j * kTileN + c;
+                    *reinterpret_cast<uint32_t *>(y) = to16<F16>(lo) | (to16<F16>(hi) << 16);
+                } else {
+                    const int col = j * kTileN + c;
+                    if (a.y_f32) {
+                        *reinterpret_cast<float2 *>(static_cast<float *>(a.y) + tok * a.ldy + col) =
+                            make_float2(v0[mt][b][h], v0[mt][b][2 + h]);
+                    } else {
+                        uint16_t *y = static_cast<uint16_t *>(a.y) + tok * a.ldy + col;
+                        *reinterpret_cast<uint32_t *>(y) = to16<F16>(v0[mt][b][h]) | (to16<F16>(v0[mt][b][2 + h]) << 16);
+                    }
+                }
+            }
+        }
     }
+}
 
-    float tot[MT][4][4];
+template <int MT>
+__device__ __forceinline__ void zero(float (&v)[MT][4][4]) {
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
         for (int b = 0; b < 4; ++b)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) tot[mt][b][i] = 0.0f;
+            for (int i = 0; i < 4; ++i) v[mt][b][i] = 0.0f;
+}
 
-    auto flush = [&](int slot) {
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-            for (int b = 0; b < 4; ++b)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    red[warp][slot][mt * 8 + 2 * t + (i & 1)][8 * g + 2 * b + (i >> 1)] = tot[mt][b][i];
-                    tot[mt][b][i] = 0.0f;
-                }
-    };
-
-    int it = warp;
-    int cur_slot = nk > 0 ? it / nk : 0;
-    TileRegs cur, nxt;
-    auto tile_ptr = [&](int item) {
-        const int slot = item / nk;
-        const int kt = kb + item - slot * nk;
-        int64_t cb = col_base[0];
-#pragma unroll
-        for (int s = 1; s < NCOL; ++s)
-            if (slot == s) cb = col_base[s];
-        return a.packed + (cb + kt) * kTileBytes;
-    };
-    if (it < items) load_tile(cur, tile_ptr(it), lane_off, g);
-    while (it < items) {
-        const int nit = it + kWarps;
-        if (nit < items) load_tile(nxt, tile_ptr(nit), lane_off, g);
-        const int slot = it / nk;
-        if (slot != cur_slot) {
-            flush(cur_slot);
-            cur_slot = slot;
-        }
-        const int kt = kb + it - slot * nk;
-        tile_mma<MT, F16>(cur, a.x, a.ldx, a.m, static_cast<int64_t>(kt) * kTileK, g, t, tot);
-        cur = nxt;
-        it = nit;
-    }
-    if (warp < items) flush(cur_slot);
-    __syncthreads();
-
-    const int n = a.n_tiles * kTileN;
-    const int total = NCOL * a.m * kTileN;
-    // Column index (within the computed n) of slot s, lane column c.
-    auto out_col = [&](int s, int c) { return (base + s * a.col_stride) * kTileN + c; };
-
-    if (a.splits > 1) {
-        for (int e = threadIdx.x; e < total; e += kThreads) {
-            const int s = e / (a.m * kTileN), tok = (e / kTileN) % a.m, c = e % kTileN;
-            float v = 0.0f;
-#pragma unroll
-            for (int w = 0; w < kWarps; ++w) v += red[w][s][tok][c];
-            a.partial[(static_cast<int64_t>(blockIdx.y) * a.m + tok) * n + out_col(s, c)] = v;
-        }
-        __threadfence();
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            const int prev = atomicAdd(&a.counters[cs], 1);
-            s_last = prev == a.splits - 1;
-        }
-        __syncthreads();
-        if (!s_last) return;
-        __threadfence();
-    }
-
-    // Sum of slot s, row tok, lane column c: from shared memory, or from all splits in order.
-    auto value = [&](int s, int tok, int c) {
-        if (a.splits == 1) {
-            float v = 0.0f;
-#pragma unroll
-            for (int w = 0; w < kWarps; ++w) v += red[w][s][tok][c];
-            return v;
-        }
-        float v = 0.0f;
-        for (int sp = 0; sp < a.splits; ++sp) v += __ldcg(a.partial + (static_cast<int64_t>(sp) * a.m + tok) * n + out_col(s, c));
-        return v;
-    };
-
-    if constexpr (EPI == HMB_EPI_SWIGLU) {
-        uint16_t *y = static_cast<uint16_t *>(a.y);
-        for (int e = threadIdx.x; e < a.m * kTileN; e += kThreads) {
-            const int tok = e / kTileN, c = e % kTileN;
-            const float act = silu_mul_rounded<F16>(value(0, tok, c), value(1, tok, c));
-            y[tok * a.ldy + cs * kTileN + c] = static_cast<uint16_t>(to16<F16>(act));
-        }
-    } else {
-        for (int e = threadIdx.x; e < total; e += kThreads) {
-            const int s = e / (a.m * kTileN), tok = (e / kTileN) % a.m, c = e % kTileN;
-            const float v = value(s, tok, c);
-            if (a.y_f32) {
-                static_cast<float *>(a.y)[tok * a.ldy + out_col(s, c)] = v;
-            } else {
-                static_cast<uint16_t *>(a.y)[tok * a.ldy + out_col(s, c)] = static_cast<uint16_t>(to16<F16>(v));
+// Walks the items of a warp chunk in order: column set j, slot s (gate/up), tile row kt.
+struct Cursor {
+    int j, s, kt;
+    __device__ __forceinline__ void next(int k_tiles, int ncol) {
+        if (++kt == k_tiles) {
+            kt = 0;
+            if (++s == ncol) {
+                s = 0;
+                ++j;
             }
         }
     }
-    if (a.splits > 1 && threadIdx.x == 0) a.counters[cs] = 0;
+};
+
+template <int NCOL, int MT, int W, int S, int MAXM, bool F16, int EPI>
+__global__ void __launch_bounds__(W * 32, 1) gemv_kernel(const GemvArgs a) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int gw = blockIdx.x * W + warp;
+    if (gw >= a.warps) return;  // a.warps <= items: every chunk below it holds at least one tile
+    const int b = static_cast<int>(static_cast<int64_t>(gw) * a.items / a.warps);
+    const int e = static_cast<int>(static_cast<int64_t>(gw + 1) * a.items / a.warps);
+    const int per_set = NCOL * a.k_tiles;
+    const int sb = stage_bytes(a.m);
+    // Stage addresses are offsets from g_smem for loads; cp.async takes the shared-window address.
+    const uint32_t smem_base = static_cast<uint32_t>(__cvta_generic_to_shared(g_smem));
+    const uint32_t ring = warp * S * sb;
+    // This lane's 16 bytes of weight chunk c are at tile + 512 c + lane_off: K rows 16c + 4t .. +3, column group g.
+    const int lane_off = 256 * (t >> 1) + 32 * g + 16 * (t & 1);
+    const uint32_t wlane = 16 * lane;
+    // Scales, zeros and x rows of a tile: 16 + 16 m copies of 16 bytes, taken by the lanes in turn.
+    // Lane copy r (r = 0, 1, ...) takes copy lane + 32 r.
+    const int meta = 16 + 16 * a.m;
+    // Per copy: destination offset in a stage, and for x rows the source offset from the tile's x.
+    int64_t meta_src[(16 + 16 * MAXM + 31) / 32];
+    uint32_t meta_dst[(16 + 16 * MAXM + 31) / 32];
+#pragma unroll
+    for (int r = 0; r < (16 + 16 * MAXM + 31) / 32; ++r) {
+        const int c = lane + 32 * r;
+        const int tok = (c - 16) >> 4, piece = (c - 16) & 15;
+        meta_dst[r] = c < 16 ? 4096 + c * 16 : 4352 + tok * kXRowBytes + piece * 16;
+        meta_src[r] = c < 16 ? 0 : (static_cast<int64_t>(tok) * a.ldx + piece * 8) * 2;
+    }
+    uint32_t xrow[MT];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) xrow[mt] = 4352 + min(mt * 8 + g, a.m - 1) * kXRowBytes + 8 * t;
+
+    auto col_tile = [&](int j, int s) {
+        const int base = (NCOL == 2 && a.col_stride == 1) ? 2 * j : j;
+        return a.col_tile0 + base + s * a.col_stride;
+    };
+    Cursor in{b / per_set, (b % per_set) / a.k_tiles, b % a.k_tiles};
+    const uint8_t *in_col = a.packed + tile_index(col_tile(in.j, in.s), 0, a.tiles_k_total, a.tiles_n_total) * kTileBytes;
+    uint32_t in_dst = ring + wlane;
+    const uint32_t ring_end = ring + S * sb;
+    auto issue = [&]() {
+        const uint8_t *tile = in_col + static_cast<int64_t>(in.kt) * kTileBytes;
+        const uint8_t *wsrc = tile + lane_off;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) cp_async16(smem_base + in_dst + c * 512, wsrc + 512 * c);
+        const uint32_t mdst = in_dst - wlane;
+        const uint8_t *xsrc = reinterpret_cast<const uint8_t *>(a.x + in.kt * kTileK);
+#pragma unroll
+        for (int r = 0; r < (16 + 16 * MAXM + 31) / 32; ++r) {
+            const int c = lane + 32 * r;
+            if (c < meta) {
+                const uint8_t *src = c < 16 ? tile + 4096 + c * 16 : xsrc + meta_src[r];
+                cp_async16(smem_base + mdst + meta_dst[r], src);
+            }
+        }
+        const int j0 = in.j, s0 = in.s;
+        in.next(a.k_tiles, NCOL);
+        if (in.j != j0 || in.s != s0) {
+            in_col = a.packed + tile_index(col_tile(in.j, in.s), 0, a.tiles_k_total, a.tiles_n_total) * kTileBytes;
+        }
+        in_dst += sb;
+        if (in_dst >= ring_end) in_dst -= S * sb;
+    };
+
+#pragma unroll
+    for (int p = 0; p < S - 1; ++p) {
+        if (b + p < e) issue();
+        cp_async_commit();
+    }
+
+    float acc[MT][4][4], gate[MT][4][4];
+    zero(acc);
+    zero(gate);
+
+    // Finish column set j from acc (slot NCOL-1) and gate (slot 0 when NCOL == 2): from registers if
+    // this chunk holds all of it, else as a contributor.
+    auto finish = [&](int j) {
+        const float(&v0)[MT][4][4] = NCOL == 2 ? gate : acc;
+        const int first = j * per_set, last = first + per_set - 1;
+        if (first >= b && last < e) {
+            epilogue<MT, F16, EPI>(a, j, g, t, v0, acc);
+            return;
+        }
+        const int c0 = chunk_of(first, a.items, a.warps), c1 = chunk_of(last, a.items, a.warps);
+        constexpr int kVals = MT * 16;
+        float *slot = a.partial + static_cast<int64_t>(gw + j) * (NCOL * kVals * 32);
+#pragma unroll
+        for (int i = 0; i < kVals; ++i) {
+            __stcg(slot + i * 32 + lane, (&v0[0][0][0])[i]);
+            if (NCOL == 2) __stcg(slot + (kVals + i) * 32 + lane, (&acc[0][0][0])[i]);
+        }
+        __threadfence();
+        __syncwarp();
+        int last_one = 0;
+        if (lane == 0) last_one = atomicAdd(a.counters + j, 1) == c1 - c0;
+        last_one = __shfl_sync(0xffffffffu, last_one, 0);
+        if (!last_one) return;
+        __threadfence();
+        float s0[MT][4][4], s1[MT][4][4];
+        zero(s0);
+        zero(s1);
+        for (int c = c0; c <= c1; ++c) {
+            const float *src = a.partial + static_cast<int64_t>(c + j) * (NCOL * kVals * 32);
+#pragma unroll
+            for (int i = 0; i < kVals; ++i) {
+                (&s0[0][0][0])[i] += __ldcg(src + i * 32 + lane);
+                if (NCOL == 2) (&s1[0][0][0])[i] += __ldcg(src + (kVals + i) * 32 + lane);
+            }
+        }
+        epilogue<MT, F16, EPI>(a, j, g, t, s0, NCOL == 2 ? s1 : s0);
+        if (lane == 0) a.counters[j] = 0;
+    };
+
+    Cursor cur{b / per_set, (b % per_set) / a.k_tiles, b % a.k_tiles};
+    int stage = 0;
+    for (int it = b; it < e; ++it) {
+        cp_async_wait<S - 2>();
+        if (it + S - 1 < e) issue();
+        cp_async_commit();
+        tile_mma<MT, F16>(ring + stage * sb, wlane, xrow, g, acc);
+        stage = stage + 1 == S ? 0 : stage + 1;
+        const int j0 = cur.j, s0 = cur.s;
+        cur.next(a.k_tiles, NCOL);
+        const bool set_done = cur.j != j0 || it + 1 == e;
+        // acc holds the slot in progress; gate sums move aside when the up tiles start or the chunk ends on them.
+        if (NCOL == 2 && s0 == 0 && (set_done || cur.s == 1)) {
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        gate[mt][q][i] = acc[mt][q][i];
+                        acc[mt][q][i] = 0.0f;
+                    }
+        }
+        if (set_done) {
+            finish(j0);
+            zero(acc);
+            zero(gate);
+        }
+    }
+    cp_async_wait<0>();
+}
+
+template <int NCOL, int MT, int W, int S, int MAXM, bool F16, int EPI>
+int launch(const GemvArgs &a, cudaStream_t stream) {
+    auto kernel = gemv_kernel<NCOL, MT, W, S, MAXM, F16, EPI>;
+    constexpr int smem = W * S * stage_bytes(MAXM);
+    static_assert(smem <= kSmemBudget, "ring too large");
+    static std::mutex mu;
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (dev < 64 && !configured[dev]) {
+            const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (e != cudaSuccess) {
+                set_cuda_error(e);
+                return HMB_ERR_CUDA;
+            }
+            configured[dev] = true;
+        }
+    }
+    kernel<<<(a.warps + W - 1) / W, W * 32, W * S * stage_bytes(a.m), stream>>>(a);
+    return launch_status();
+}
+
+// Ring depth by rows of x: stage_bytes grows with m, the ring stays within the shared-memory budget.
+template <int NCOL, bool F16, int EPI>
+int by_rows(const GemvArgs &a, cudaStream_t stream) {
+    if (a.m == 1) return launch<NCOL, 1, 16, 3, 1, F16, EPI>(a, stream);
+    if (a.m == 2) return launch<NCOL, 1, 8, 5, 2, F16, EPI>(a, stream);
+    if (a.m <= 8) return launch<NCOL, 1, 8, 4, 8, F16, EPI>(a, stream);
+    return launch<NCOL, 2, 8, 3, 16, F16, EPI>(a, stream);
+}
+
+template <bool F16>
+int dispatch(const GemvArgs &a, int epilogue, cudaStream_t stream) {
+    if (epilogue == HMB_EPI_SWIGLU) return by_rows<2, F16, HMB_EPI_SWIGLU>(a, stream);
+    return by_rows<1, F16, HMB_EPI_STORE>(a, stream);
+}
+
+// Warps per CTA for m rows of x (the kernel variant by_rows() picks).
+int warps_per_cta(int64_t m) { return m == 1 ? 16 : 8; }
+
+// Warps that share the tile stream: those of one CTA per SM (split_k > 0 caps the CTAs), never more
+// than there are tiles.
+int64_t grid_warps(int64_t items, int split_k, int64_t m) {
+    int64_t ctas = sm_count();
+    if (split_k > 0) ctas = std::min<int64_t>(ctas, split_k);
+    return std::max<int64_t>(1, std::min<int64_t>(ctas * warps_per_cta(m), items));
 }
 
 constexpr size_t kCounterBytes = 64 * 1024;  // room for 16384 column sets
 
-int pick_splits(int colsets, int k_tiles, int ncol) {
-    const int target = 4 * sm_count();
-    int splits = (target + colsets - 1) / colsets;
-    // Keep at least one tile per warp in every split.
-    splits = std::min(splits, std::max(1, ncol * k_tiles / kWarps));
-    return std::max(1, std::min(splits, k_tiles));
-}
-
-template <int NCOL, int MT, bool F16, int EPI>
-int launch(const GemvArgs &a, int colsets, cudaStream_t stream) {
-    gemv_kernel<NCOL, MT, F16, EPI><<<dim3(colsets, a.splits), kThreads, 0, stream>>>(a);
-    return launch_status();
-}
-
-template <bool F16>
-int dispatch(const GemvArgs &a, int colsets, int epilogue, cudaStream_t stream) {
-    if (epilogue == HMB_EPI_SWIGLU) {
-        return a.m <= 8 ? launch<2, 1, F16, HMB_EPI_SWIGLU>(a, colsets, stream)
-                        : launch<2, 2, F16, HMB_EPI_SWIGLU>(a, colsets, stream);
-    }
-    return a.m <= 8 ? launch<1, 1, F16, HMB_EPI_STORE>(a, colsets, stream) : launch<1, 2, F16, HMB_EPI_STORE>(a, colsets, stream);
+size_t partial_bytes(int64_t m, int64_t colsets, int ncol, int64_t warps) {
+    const int mt = m <= 8 ? 1 : 2;
+    return static_cast<size_t>(warps + colsets) * ncol * mt * 16 * 32 * sizeof(float);
 }
 
 }  // namespace
@@ -320,11 +469,9 @@ extern "C" {
 size_t hmb_w4a16_gemv_workspace(int64_t m, int64_t k, int64_t n, int epilogue, int split_k) {
     if (m <= 0 || k <= 0 || n <= 0 || k % kTileK || n % kTileN) return 0;
     const int ncol = epilogue == HMB_EPI_SWIGLU ? 2 : 1;
-    const int k_tiles = static_cast<int>(k / kTileK);
-    const int colsets = static_cast<int>(n / kTileN) / ncol;
-    const int splits = split_k > 0 ? std::min(split_k, k_tiles) : pick_splits(colsets, k_tiles, ncol);
-    const int64_t rows = std::min<int64_t>(m, 16);
-    return kCounterBytes + static_cast<size_t>(splits) * rows * n * sizeof(float);
+    const int64_t colsets = (n / kTileN) / ncol;
+    const int64_t items = colsets * ncol * (k / kTileK);
+    return kCounterBytes + partial_bytes(std::min<int64_t>(m, 16), colsets, ncol, grid_warps(items, split_k, std::min<int64_t>(m, 16)));
 }
 
 int hmb_w4a16_gemv(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const void *x, int64_t ldx, int x_dtype, void *y,
@@ -352,30 +499,29 @@ int hmb_w4a16_gemv(const uint8_t *packed, int64_t packed_k, int64_t packed_n, co
     a.tiles_n_total = static_cast<int>(packed_n / kTileN);
     a.col_tile0 = static_cast<int>(start_col / kTileN);
     a.k_tiles = static_cast<int>(k / kTileK);
-    a.n_tiles = static_cast<int>(n / kTileN);
+    const int n_tiles = static_cast<int>(n / kTileN);
     a.ldx = ldx;
     a.ldy = ldy;
     a.y_f32 = y_dtype == HMB_FP32;
     const int ncol = epilogue == HMB_EPI_SWIGLU ? 2 : 1;
-    const int colsets = a.n_tiles / ncol;
-    a.col_stride = epilogue == HMB_EPI_SWIGLU ? (layout == HMB_GATE_UP_INTERLEAVED ? 1 : a.n_tiles / 2) : 0;
-    a.splits = split_k > 0 ? std::min<int>(split_k, a.k_tiles) : pick_splits(colsets, a.k_tiles, ncol);
-    a.tiles_per_split = (a.k_tiles + a.splits - 1) / a.splits;
-    a.splits = (a.k_tiles + a.tiles_per_split - 1) / a.tiles_per_split;
-    if (colsets > static_cast<int>(kCounterBytes / sizeof(int))) return HMB_ERR_UNSUPPORTED;
-    if (a.splits > 1) {
-        const size_t need = kCounterBytes + static_cast<size_t>(a.splits) * std::min<int64_t>(m, 16) * n * sizeof(float);
-        if (!workspace || workspace_bytes < need || !aligned(workspace, 16)) return HMB_ERR_WORKSPACE;
-        a.counters = static_cast<int *>(workspace);
-        a.partial = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + kCounterBytes);
-    }
+    a.colsets = n_tiles / ncol;
+    a.col_stride = epilogue == HMB_EPI_SWIGLU ? (layout == HMB_GATE_UP_INTERLEAVED ? 1 : n_tiles / 2) : 0;
+    const int64_t items = static_cast<int64_t>(a.colsets) * ncol * a.k_tiles;
+    if (items > (1LL << 30)) return HMB_ERR_UNSUPPORTED;
+    a.items = static_cast<int>(items);
+    a.warps = static_cast<int>(grid_warps(items, split_k, std::min<int64_t>(m, 16)));
+    if (a.colsets > static_cast<int>(kCounterBytes / sizeof(int))) return HMB_ERR_UNSUPPORTED;
+    const size_t need = kCounterBytes + partial_bytes(std::min<int64_t>(m, 16), a.colsets, ncol, a.warps);
+    if (!workspace || workspace_bytes < need || !aligned(workspace, 16)) return HMB_ERR_WORKSPACE;
+    a.counters = static_cast<int *>(workspace);
+    a.partial = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + kCounterBytes);
+
     const size_t y_elem = y_dtype == HMB_FP32 ? 4 : 2;
     for (int64_t r0 = 0; r0 < m; r0 += 16) {
         a.m = static_cast<int>(std::min<int64_t>(16, m - r0));
         a.x = static_cast<const uint16_t *>(x) + r0 * ldx;
         a.y = static_cast<uint8_t *>(y) + r0 * ldy * y_elem;
-        const int rc = x_dtype == HMB_FP16 ? dispatch<true>(a, colsets, epilogue, stream)
-                                           : dispatch<false>(a, colsets, epilogue, stream);
+        const int rc = x_dtype == HMB_FP16 ? dispatch<true>(a, epilogue, stream) : dispatch<false>(a, epilogue, stream);
         if (rc != HMB_OK) return rc;
     }
     return HMB_OK;

@@ -29,17 +29,18 @@ def assert_close(got, ref, tol=LEVEL, what=""):
     return max_rel, rel_l2, cos
 
 
-def assert_bf16_close(got_bits, ref_bits, max_ulp=1, min_equal=0.99, what=""):
-    """Two bf16 bit arrays from the same arithmetic in a different summation order: at most
-    `max_ulp` apart everywhere and identical in at least `min_equal` of the elements."""
-    g = np.asarray(got_bits, np.uint16).astype(np.int32).ravel()
-    r = np.asarray(ref_bits, np.uint16).astype(np.int32).ravel()
-    # Map sign-magnitude bf16 to a monotonic integer line.
-    g = np.where(g & 0x8000, -(g & 0x7FFF), g)
-    r = np.where(r & 0x8000, -(r & 0x7FFF), r)
-    d = np.abs(g - r)
-    eq = float(np.mean(d == 0))
-    assert d.max() <= max_ulp and eq >= min_equal, f"{what}: max ulp {d.max()}, equal {eq:.4f}"
+def assert_bf16_close(got_bits, ref_bits, max_rel=2.0 ** -8, min_equal=0.99, what=""):
+    """Two bf16 bit arrays from the same arithmetic in a different summation order: identical in at
+    least `min_equal` of the elements, and no element further from the reference than `max_rel`
+    times max|ref| (one bf16 ulp at the largest magnitude by default). A per-element ulp bound
+    does not hold where a sum cancels to a small value."""
+    g = np.asarray(got_bits, np.uint16).ravel()
+    r = np.asarray(ref_bits, np.uint16).ravel()
+    gf = (g.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    rf = (r.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    eq = float(np.mean(g == r))
+    rel = float(np.abs(gf - rf).max() / (np.abs(rf).max() + 1e-30))
+    assert rel <= max_rel and eq >= min_equal, f"{what}: max_rel {rel:.2e}, equal {eq:.4f}"
     return eq
 
 

@@ -109,7 +109,7 @@ def test_full_size_sampled_columns(cuda, oracle, hidden, inter):
         # channels c0 .. c0+63: gate tile column 2*(c0/64), up tile column +1 (interleaved)
         _, gate_up = oracle.gemv(gu_h, hidden, 2 * inter, x, n=128, n0=2 * c0)
         ref_act = oracle.silu_mul(gate_up, 64, 1)
-        assert_bf16_close(act_bits[:, c0:c0 + 64], ref_act, max_ulp=2, min_equal=0.95, what=f"act @{c0}")
+        assert_bf16_close(act_bits[:, c0:c0 + 64], ref_act, min_equal=0.95, what=f"act @{c0}")
     for c0 in (0, hidden - 128, hidden // 2):
         y32, _ = oracle.gemv(dn_h, inter, hidden, act_bits, n=128, n0=c0)
         assert_close(y_h[:, c0:c0 + 128], y32, (1e-5, 1e-5, 0.9999999), f"down @{c0}")

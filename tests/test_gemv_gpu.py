@@ -42,7 +42,7 @@ def test_gemv_matches_oracle(cuda, oracle, k, n, m):
     y = torch.empty(m, n, dtype=torch.bfloat16, device=cuda)
     ops.w4a16_gemv(y, to_dev_bf16(x, cuda), torch.from_numpy(p).to(cuda), k, n, k, n, 0, 0, 0, 0)
     torch.cuda.synchronize()
-    assert_bf16_close(bits_of(y), y16, max_ulp=1, min_equal=0.97, what=f"gemv k={k} n={n} m={m}")
+    assert_bf16_close(bits_of(y), y16, min_equal=0.97, what=f"gemv k={k} n={n} m={m}")
 
 
 @pytest.mark.parametrize("split", [0, 1, 2, 3, 8, 64])
@@ -54,7 +54,7 @@ def test_gemv_split_k(cuda, oracle, split):
     y = torch.empty(1, n, dtype=torch.bfloat16, device=cuda)
     H.gemv_w4a16(y, to_dev_bf16(x, cuda)[0], torch.from_numpy(p).to(cuda), k, n, k, n, split)
     torch.cuda.synchronize()
-    assert_bf16_close(bits_of(y), y16, max_ulp=1, min_equal=0.97, what=f"split {split}")
+    assert_bf16_close(bits_of(y), y16, min_equal=0.97, what=f"split {split}")
     # fp32 output: unrounded sums
     y_f = torch.empty(1, n, dtype=torch.float32, device=cuda)
     ops.w4a16_gemv(y_f, to_dev_bf16(x, cuda), torch.from_numpy(p).to(cuda), k, n, k, n, 0, 0, 0, split)
@@ -75,7 +75,7 @@ def test_gemv_leading_block_and_start_col(cuda, oracle):
             y = torch.empty(m, n, dtype=torch.bfloat16, device=cuda)
             ops.w4a16_gemv(y, to_dev_bf16(x, cuda), pd, k, n, pk, pn, start, 0, 0, 0)
             torch.cuda.synchronize()
-            assert_bf16_close(bits_of(y), y16, max_ulp=1, min_equal=0.97, what=f"block {k}x{n}@{start} m={m}")
+            assert_bf16_close(bits_of(y), y16, min_equal=0.97, what=f"block {k}x{n}@{start} m={m}")
 
 
 @pytest.mark.parametrize("layout", [0, 1])
@@ -89,7 +89,7 @@ def test_gemv_swiglu_epilogue(cuda, oracle, layout, m):
     act = torch.empty(m, c, dtype=torch.bfloat16, device=cuda)
     ops.w4a16_gemv(act, to_dev_bf16(x, cuda), torch.from_numpy(p).to(cuda), h, 2 * c, h, 2 * c, 0, 1, layout, 0)
     torch.cuda.synchronize()
-    assert_bf16_close(bits_of(act), act_ref, max_ulp=2, min_equal=0.97, what=f"swiglu layout={layout} m={m}")
+    assert_bf16_close(bits_of(act), act_ref, min_equal=0.97, what=f"swiglu layout={layout} m={m}")
 
 
 def test_gemv_fp16_activations(cuda, oracle):
@@ -154,7 +154,7 @@ def test_silu_mul_and_residual_add2(cuda, oracle):
             act = torch.empty(m, n, dtype=torch.bfloat16, device=cuda)
             H.silu_mul(to_dev_bf16(gu, cuda), act, layout=H.GateUpLayout(layout))
             torch.cuda.synchronize()
-            assert_bf16_close(bits_of(act), oracle.silu_mul(gu, n, layout), max_ulp=1, min_equal=0.99,
+            assert_bf16_close(bits_of(act), oracle.silu_mul(gu, n, layout), min_equal=0.99,
                               what=f"silu_mul m={m} layout={layout}")
     for m in (1, 300):
         h = 4096

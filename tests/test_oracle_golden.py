@@ -43,11 +43,11 @@ def test_gemv_matches_reference_avx_fixture(oracle, golden):
     for key in ("k256_n384", "k1024_n256", "k2048_n128"):
         k, n = (int(v[1:]) for v in key.split("_"))
         y32, y16 = oracle.gemv(g[key + "_packed"], k, n, g[key + "_x"][None])
-        assert_bf16_close(y16[0], g[key + "_avx"], max_ulp=1, min_equal=0.98, what=key)
+        assert_bf16_close(y16[0], g[key + "_avx"], min_equal=0.98, what=key)
         rel = np.abs(y32[0] - g[key + "_f64"]).max() / np.abs(g[key + "_f64"]).max()
         assert rel < 1e-5, key
         _, part = oracle.gemv(g[key + "_packed"], k, n, g[key + "_x"][None], n=128, n0=n - 128)
-        assert_bf16_close(part[0], g[key + "_avx_lastcols"], max_ulp=1, min_equal=0.98, what=key + " cols")
+        assert_bf16_close(part[0], g[key + "_avx_lastcols"], min_equal=0.98, what=key + " cols")
 
 
 def test_ffn_matches_reference_cpu_chain(oracle, golden):
@@ -56,7 +56,7 @@ def test_ffn_matches_reference_cpu_chain(oracle, golden):
     # The reference packs gate and up separately; the oracle takes the blocked gate_up concatenation.
     gate_up = oracle.pack(*_concat_unpacked(oracle, g["gate"], g["up"], h, inter))
     y16, y32 = oracle.ffn(gate_up, g["down"], h, inter, inter, 0, g["x"])
-    assert_bf16_close(y16, g["avx_chain"], max_ulp=2, min_equal=0.95, what="ffn vs AVX chain")
+    assert_bf16_close(y16, g["avx_chain"], min_equal=0.95, what="ffn vs AVX chain")
     # The float oracle of npu/ffn/reference.py keeps everything fp32: same values within LEVEL.
     assert_close(y32, g["f32"], LEVEL, "ffn vs fp32 reference oracle")
     # Partition algebra: the two partials of the reference's split add up to its full result.
@@ -100,4 +100,4 @@ def test_oracle_against_reference_build(oracle):
     p = oracle.pack(q, s, z)
     x = oracle.bf16_bits(rng.standard_normal(k))
     _, y16 = oracle.gemv(p, k, n, x[None])
-    assert_bf16_close(y16[0], ref.gemv(x, p, k, n, threads=2), max_ulp=1, min_equal=0.98, what="oracle vs reference AVX")
+    assert_bf16_close(y16[0], ref.gemv(x, p, k, n, threads=2), min_equal=0.98, what="oracle vs reference AVX")
