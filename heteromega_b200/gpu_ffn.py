@@ -25,7 +25,7 @@ import torch
 
 from . import _lib
 from ._lib import check, lib
-from .torch_ops import ops
+from .torch_ops import ops, w4a16_linear
 
 kTileK = _lib.TILE_K
 kTileN = _lib.TILE_N
@@ -271,7 +271,7 @@ def gemv_w4a16(out, x, packed, k, n, packed_k, packed_n, split_k=0, stream=None)
 
 def _linear(out, x, packed, k, n, pk, pn, fuse_activation=False, layout=GateUpLayout.kInterleaved, split_k=0):
     epi = _lib.HMB_EPI_SWIGLU if fuse_activation else _lib.HMB_EPI_STORE
-    ops.w4a16_gemv(out, x, packed, k, n, pk, pn, 0, epi, int(layout), int(split_k))
+    w4a16_linear(out, x, packed, k, n, pk, pn, 0, epi, int(layout), int(split_k))
 
 
 def gemm_w4a16_supports(m, k, n):
@@ -339,8 +339,8 @@ def gpu_ffn_slice_forward(w, x_norm, buf, y, stream=None):
         raise ValueError("gpu_ffn_slice_forward: y must be [M, H]")
     with _stream_ctx(stream):
         act = _act_buffer(buf, m, n, x_norm.device)
-        ops.w4a16_gemv(act, x_norm, w.gate_up, h, 2 * n, h, 2 * stored, 0, _lib.HMB_EPI_SWIGLU, int(w.layout), 0)
-        ops.w4a16_gemv(y, act, w.down, n, h, stored, h, 0, _lib.HMB_EPI_STORE, 0, 0)
+        w4a16_linear(act, x_norm, w.gate_up, h, 2 * n, h, 2 * stored, 0, _lib.HMB_EPI_SWIGLU, int(w.layout))
+        w4a16_linear(y, act, w.down, n, h, stored, h, 0, _lib.HMB_EPI_STORE)
 
 
 def packed_linear(out, inp, packed, k, n, stream=None, opt=None):

@@ -15,7 +15,7 @@ import torch.distributed as dist
 from . import _lib
 from .gpu_ffn import FfnSliceWeights, GateUpLayout, slice_packed_ffn
 from .partition import plan_shards
-from .torch_ops import ops
+from .torch_ops import w4a16_linear
 
 
 class TensorParallelFfn:
@@ -56,8 +56,8 @@ class TensorParallelFfn:
         m = x.shape[0]
         if act is None:
             act = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
-        ops.w4a16_gemv(act, x, w.gate_up, h, 2 * n, h, 2 * stored, 0, _lib.HMB_EPI_SWIGLU, int(w.layout), 0)
-        ops.w4a16_gemv(partial, act, w.down, n, h, stored, h, 0, _lib.HMB_EPI_STORE, 0, 0)
+        w4a16_linear(act, x, w.gate_up, h, 2 * n, h, 2 * stored, 0, _lib.HMB_EPI_SWIGLU, int(w.layout))
+        w4a16_linear(partial, act, w.down, n, h, stored, h, 0, _lib.HMB_EPI_STORE)
         return partial
 
     def reduce_partials(self, partial):

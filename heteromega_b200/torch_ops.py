@@ -68,6 +68,8 @@ def _check_cuda(*ts):
 _defs = torch.library.Library("heteromega", "DEF")
 _defs.define("w4a16_gemv(Tensor(a!) out, Tensor x, Tensor packed, int k, int n, int packed_k, int packed_n, "
              "int start_col, int epilogue, int layout, int split_k) -> ()")
+_defs.define("w4a16_gemm(Tensor(a!) out, Tensor x, Tensor packed, int k, int n, int packed_k, int packed_n, "
+             "int start_col, int epilogue, int layout) -> ()")
 _defs.define("w4a16_dequant(Tensor(a!) out, Tensor packed, int k, int n, int packed_k, int packed_n) -> ()")
 _defs.define("silu_mul(Tensor gate_up, Tensor(a!) act, int layout) -> ()")
 _defs.define("residual_add2(Tensor(a!) x, Tensor y_g, Tensor y_n) -> ()")
@@ -91,6 +93,49 @@ def _w4a16_gemv(out, x, packed, k, n, packed_k, packed_n, start_col, epilogue, l
     check(lib().hmb_w4a16_gemv(packed.data_ptr(), packed_k, packed_n, x.data_ptr(), _ld(x), _dtype_code(x), out.data_ptr(),
                                _ld(out), _dtype_code(out), m, k, n, start_col, epilogue, layout, split_k, ws.data_ptr(),
                                ws.numel(), _stream(x)), "w4a16_gemv")
+
+
+def _w4a16_gemm(out, x, packed, k, n, packed_k, packed_n, start_col, epilogue, layout):
+    _check_cuda(out, x, packed)
+    if x.dim() != 2 or out.dim() != 2 or x.stride(1) != 1 or out.stride(1) != 1:
+        raise ValueError("w4a16_gemm: x and out must be [M, K] / [M, N] with contiguous rows")
+    m = x.shape[0]
+    if out.shape[0] != m:
+        raise ValueError("w4a16_gemm: x and out must have the same number of rows")
+    if out.dtype != x.dtype:
+        raise ValueError("w4a16_gemm: out must have the activation dtype")
+    if packed.dtype != torch.uint8 or not packed.is_contiguous():
+        raise ValueError("w4a16_gemm: packed must be contiguous uint8")
+    if packed.numel() != lib().hmb_packed_bytes(packed_k, packed_n):
+        raise ValueError(f"w4a16_gemm: packed has {packed.numel()} bytes, not those of [{packed_k}, {packed_n}]")
+    check(lib().hmb_w4a16_gemm(packed.data_ptr(), packed_k, packed_n, x.data_ptr(), x.stride(0), _dtype_code(x),
+                               out.data_ptr(), out.stride(0), m, k, n, start_col, epilogue, layout, _stream(x)), "w4a16_gemm")
+
+
+def gemm_supported(m, k, n, epilogue):
+    return bool(lib().hmb_w4a16_gemm_supports(m, k, n, epilogue))
+
+
+# Rows above which the tensor-core GEMM takes over from the decode GEMV.
+GEMV_MAX_ROWS = 16
+
+
+def w4a16_linear(out, x, packed, k, n, packed_k, packed_n, start_col=0, epilogue=0, layout=1, split_k=0):
+    """The product's packed matmul: the decode GEMV for m <= GEMV_MAX_ROWS, the tcgen05 GEMM above it
+    when the shape allows, else the GEMV over row chunks."""
+    m = x.shape[0] if x.dim() == 2 else 1
+    if m > GEMV_MAX_ROWS and out.dtype == x.dtype and gemm_supported(m, k, n, epilogue):
+        ops.w4a16_gemm(out, x, packed, k, n, packed_k, packed_n, start_col, epilogue, layout)
+    else:
+        ops.w4a16_gemv(out, x, packed, k, n, packed_k, packed_n, start_col, epilogue, layout, split_k)
+
+
+def device_status(device=None):
+    """HMB_OK, or HMB_ERR_TIMEOUT if a kernel gave up a bounded wait since the last call (clears it)."""
+    import ctypes
+    v = ctypes.c_int(0)
+    check(lib().hmb_device_status(ctypes.addressof(v), torch.cuda.current_stream(device).cuda_stream), "device_status")
+    return v.value
 
 
 def _w4a16_dequant(out, packed, k, n, packed_k, packed_n):
@@ -152,6 +197,7 @@ def _pack_w4a16_device(out, q, scales, zeros, bad):
 
 _impls = torch.library.Library("heteromega", "IMPL", "CUDA")
 _impls.impl("w4a16_gemv", _w4a16_gemv)
+_impls.impl("w4a16_gemm", _w4a16_gemm)
 _impls.impl("w4a16_dequant", _w4a16_dequant)
 _impls.impl("silu_mul", _silu_mul)
 _impls.impl("residual_add2", _residual_add2)

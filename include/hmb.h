@@ -110,8 +110,8 @@ int hmb_pack_w4a16_device(const uint8_t *q, const uint16_t *scales_bf16, const u
 int hmb_w4a16_dequant(const uint8_t *packed, int64_t packed_k, int64_t packed_n, int64_t k, int64_t n, float *out, int64_t ldo,
                       hmb_stream_t stream);
 
-/* Decode GEMV / skinny GEMM on CUDA-core-free tensor-core fragments (mma.sync), for m <= 16 per
- * launch (larger m is processed in chunks of 16 rows):
+/* Decode GEMV / skinny GEMM (in-register dequantization, mma.sync tensor-core fragments), for m <= 16
+ * per launch (larger m is processed in chunks of 16 rows):
  *   HMB_EPI_STORE:  y[m, n] = x[m, k] @ W[:k, start_col : start_col + n]
  *   HMB_EPI_SWIGLU: W[:k, start_col : start_col + n] is gate_up of n/2 channels in `layout` order and
  *                   y[m, n/2] = bf16(SiLU(g) * u) with g, u the bf16-rounded gate and up sums.
@@ -124,6 +124,21 @@ int hmb_w4a16_gemv(const uint8_t *packed, int64_t packed_k, int64_t packed_n, co
                    int64_t ldy, int y_dtype, int64_t m, int64_t k, int64_t n, int64_t start_col, int epilogue, int layout,
                    int split_k, void *workspace, size_t workspace_bytes, hmb_stream_t stream);
 size_t hmb_w4a16_gemv_workspace(int64_t m, int64_t k, int64_t n, int epilogue, int split_k);
+
+/* Prefill GEMM on the tcgen05 tensor cores (TMA-fed, TMEM accumulator), same operands and epilogues
+ * as hmb_w4a16_gemv: the weights are dequantized to bf16((q - z) * s) in shared memory, products
+ * accumulate in fp32, the output rounds once. Needs n % 256 == 0 (HMB_ERR_UNSUPPORTED otherwise,
+ * see hmb_w4a16_gemm_supports); any m. Replaces hipkernels::w4a16_gemm_fused_packed and
+ * w4a16_gemm_fused_packed_tiles with fuse_activation (include/hipkernels/w4a16_gemm_packed.hpp:38-48) and
+ * heteromega::gemm_w4a16 (gpu_ffn.hpp:101-107). */
+int hmb_w4a16_gemm(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const void *x, int64_t ldx, int x_dtype, void *y,
+                   int64_t ldy, int64_t m, int64_t k, int64_t n, int64_t start_col, int epilogue, int layout,
+                   hmb_stream_t stream);
+int hmb_w4a16_gemm_supports(int64_t m, int64_t k, int64_t n, int epilogue);
+
+/* Reads and clears the device status word of the current device: *status = HMB_ERR_TIMEOUT if a kernel
+ * gave up a bounded wait since the last call, else HMB_OK. Synchronizes `stream`. */
+int hmb_device_status(int *status, hmb_stream_t stream);
 
 /* act[m, n] = bf16(SiLU(g) * u), fp32 math, one rounding; gate_up [m, 2n] in `layout` order.
  * Replaces heteromega::silu_mul (gpu_ffn.hpp:92-93; silu_mul.cu:34-57). */
