@@ -266,7 +266,9 @@ def run_hmb(args):
     e2e = end_to_end(stack, x_all, m, args, flush, barrier, world, dev)
 
     pk, pk_kind = peaks()
-    decode = m <= 64
+    from heteromega_b200.torch_ops import GEMV_MAX_ROWS
+
+    decode = m <= GEMV_MAX_ROWS
     if decode:
         achieved = dom["bytes"] / (dom["ms"] * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
@@ -312,13 +314,13 @@ def dominant_kernel(stack, w, x, flush, stream, m, reps=20):
     import torch
 
     from heteromega_b200 import _lib
-    from heteromega_b200.torch_ops import ops
+    from heteromega_b200.torch_ops import w4a16_linear
 
     n, stored, h = w.channels(), w.stored_channels(), w.hidden
     act = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
 
     def launch():
-        ops.w4a16_gemv(act, x, w.gate_up, h, 2 * n, h, 2 * stored, 0, _lib.HMB_EPI_SWIGLU, int(w.layout), 0)
+        w4a16_linear(act, x, w.gate_up, h, 2 * n, h, 2 * stored, 0, _lib.HMB_EPI_SWIGLU, int(w.layout))
 
     launch()
     g = torch.cuda.CUDAGraph()
@@ -335,7 +337,10 @@ def dominant_kernel(stack, w, x, flush, stream, m, reps=20):
         torch.cuda.synchronize()
         times.append(s.elapsed_time(e))
     ms = statistics.median(times)
-    return {"name": "gemv_kernel<swiglu> (gate/up + SiLU*up)" if m <= 64 else "gate/up GEMM + SiLU*up", "ms": ms,
+    from heteromega_b200.torch_ops import GEMV_MAX_ROWS
+
+    return {"name": "gemv_kernel<swiglu> (gate/up + SiLU*up)" if m <= GEMV_MAX_ROWS else "gemm_kernel<swiglu> (tcgen05 gate/up + SiLU*up)",
+            "ms": ms,
             "bytes": h * 2 * n * BYTES_PER_WEIGHT + m * h * 2 + m * n * 2, "flops": 2.0 * m * h * 2 * n}
 
 

@@ -30,17 +30,28 @@
 namespace hmb {
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int kStages = 3;
-constexpr int kABytes = BM * BK * 2;            // 16384
-constexpr int kBBytes = BN * BK * 2;            // 32768
-constexpr int kPHalf = 2048 + 256;              // half a packed tile + its scales and zeros
-constexpr int kPBytes = 4 * kPHalf;             // 9216
-constexpr int kStageBytes = kABytes + kBBytes + kPBytes;  // 58368 = 57 x 1024
+constexpr int BN = 256, BK = 64;
+constexpr int kBStages = 2;            // dequantized B tiles
+constexpr int kBBytes = BN * BK * 2;   // 32768
+constexpr int kPHalf = 2048 + 256;     // half a packed tile + its scales and zeros
+constexpr int kPBytes = 4 * kPHalf;    // 9216
 constexpr int kDequantWarps = 8;
 constexpr int kThreads = (2 + kDequantWarps) * 32;
-constexpr int kTmemCols = 256;
-constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 256;
+
+// Shared-memory plan for a CTA of BM rows (BM = 128: one accumulator, BM = 256: two that share each
+// dequantized B tile, so the dequantization work per MMA halves).
+template <int BM>
+struct Plan {
+    static constexpr int kAcc = BM / 128;
+    static constexpr int kLoadStages = BM == 128 ? 5 : 3;  // x tile + packed halves, ahead of the MMA
+    static constexpr int kABytes = BM * BK * 2;
+    static constexpr int kAOff = 0;
+    static constexpr int kPOff = kAOff + kLoadStages * kABytes;
+    static constexpr int kBOff = kPOff + kLoadStages * kPBytes;  // 1024-aligned: 9216 = 9 x 1024
+    static constexpr int kBarOff = kBOff + kBStages * kBBytes;
+    static constexpr int kTmemCols = 256 * kAcc;
+    static constexpr int kSmemBytes = 1024 + kBarOff + 256;
+};
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // a barrier wait gives up after one second
 
 // Set to 1 by a kernel that gave up a bounded wait; read and cleared by hmb_device_status().
@@ -165,18 +176,23 @@ __device__ __forceinline__ uint32_t sub_mul2(uint32_t h, uint32_t zc, uint32_t s
 
 // ---- the kernel -----------------------------------------------------------------------------------
 
-template <bool F16, int EPI>
+template <int BM, bool F16, int EPI>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmArgs a) {
+    using P = Plan<BM>;
+    constexpr int kLoadStages = P::kLoadStages, kABytes = P::kABytes, kAOff = P::kAOff, kPOff = P::kPOff, kBOff = P::kBOff,
+                  kBarOff = P::kBarOff, kTmemCols = P::kTmemCols, kAcc = P::kAcc;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t bars = sbase + kStages * kStageBytes;
-    // barriers: full_load[S], full_mma[S], empty[S], acc_full; then the TMEM address and the abort flag
+    const uint32_t bars = sbase + kBarOff;
+    // barriers: full_load, empty_load (per load stage), full_b, empty_b (per B stage), acc_full;
+    // then the TMEM address and the abort flag
     auto full_load = [&](int s) { return bars + 8 * s; };
-    auto full_mma = [&](int s) { return bars + 8 * (kStages + s); };
-    auto empty = [&](int s) { return bars + 8 * (2 * kStages + s); };
-    const uint32_t acc_full = bars + 8 * (3 * kStages);
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kStages * kStageBytes + 8 * (3 * kStages + 1));
+    auto empty_load = [&](int s) { return bars + 8 * (kLoadStages + s); };
+    auto full_b = [&](int s) { return bars + 8 * (2 * kLoadStages + s); };
+    auto empty_b = [&](int s) { return bars + 8 * (2 * kLoadStages + kBStages + s); };
+    const uint32_t acc_full = bars + 8 * (2 * kLoadStages + 2 * kBStages);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kBarOff + 8 * (2 * kLoadStages + 2 * kBStages + 1));
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -192,10 +208,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     };
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < kLoadStages; ++s) {
             mbar_init(full_load(s), 1);
-            mbar_init(full_mma(s), kDequantWarps);
-            mbar_init(empty(s), 1);
+            mbar_init(empty_load(s), 1 + kDequantWarps);  // the MMA commit (x read) and every dequant warp (packed read)
+        }
+        for (int s = 0; s < kBStages; ++s) {
+            mbar_init(full_b(s), kDequantWarps);
+            mbar_init(empty_b(s), 1);
         }
         mbar_init(acc_full, 1);
         *abort = 0;
@@ -219,46 +238,47 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             for (int d = 0; d < 4; ++d) col_base[d] = a.packed + tile_index(tile_col(d), 0, a.tiles_k_total, a.tiles_n_total) * kTileBytes;
             int issued = 0;
             for (int i = 0; i < num_k; ++i) {
-                const int s = i % kStages, u = i / kStages;
-                if (u > 0 && !mbar_wait(empty(s), (u - 1) & 1, abort)) break;
-                const uint32_t st = sbase + s * kStageBytes;
+                const int s = i % kLoadStages, u = i / kLoadStages;
+                if (u > 0 && !mbar_wait(empty_load(s), (u - 1) & 1, abort)) break;
                 mbar_expect_tx(full_load(s), kABytes + kPBytes);
-                tma_load_2d(st, &tmap_x, i * BK, m0, full_load(s));
+                tma_load_2d(sbase + kAOff + s * kABytes, &tmap_x, i * BK, m0, full_load(s));
                 const int kt = i >> 1, h = i & 1;
                 for (int d = 0; d < 4; ++d) {
                     const uint8_t *tile = col_base[d] + static_cast<int64_t>(kt) * kTileBytes;
-                    const uint32_t pd = st + kABytes + kBBytes + d * kPHalf;
+                    const uint32_t pd = sbase + kPOff + s * kPBytes + d * kPHalf;
                     bulk_load(pd, tile + h * 2048, 2048, full_load(s));
                     bulk_load(pd + 2048, tile + 4096, 256, full_load(s));
                 }
                 issued = i + 1;
             }
             // Do not leave while copies of this CTA are in flight (bounded).
-            for (int i = std::max(0, issued - kStages); i < issued; ++i) {
-                mbar_wait(full_load(i % kStages), (i / kStages) & 1, abort);
+            for (int i = std::max(0, issued - kLoadStages); i < issued; ++i) {
+                mbar_wait(full_load(i % kLoadStages), (i / kLoadStages) & 1, abort);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             // MMA issuer. idesc: fp32 accumulate, bf16 (fp16) A and B, A K-major, B MN-major, N = 256, M = 128.
             const uint32_t fmt = F16 ? 0u : 1u;
-            const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 16) | ((BN >> 3) << 17) | ((BM >> 4) << 24);
-            bool ok = true;
-            for (int i = 0; i < num_k && ok; ++i) {
-                const int s = i % kStages, u = i / kStages;
-                if (!mbar_wait(full_mma(s), u & 1, abort)) {
-                    ok = false;
-                    break;
-                }
+            const uint32_t idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (1u << 16) | ((BN >> 3) << 17) | ((128 >> 4) << 24);
+            for (int i = 0; i < num_k; ++i) {
+                const int sb = i % kBStages, ub = i / kBStages;
+                if (!mbar_wait(full_b(sb), ub & 1, abort)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t st = sbase + s * kStageBytes;
+                const uint32_t sa = sbase + kAOff + (i % kLoadStages) * kABytes;
+                const uint32_t sbb = sbase + kBOff + sb * kBBytes;
 #pragma unroll
                 for (int kk = 0; kk < BK / 16; ++kk) {
-                    const uint64_t ad = smem_desc(st + kk * 32, 16, 1024);
-                    const uint64_t bd = smem_desc(st + kABytes + kk * 2 * 4096, 1024, 4096);
-                    umma_f16(tmem, ad, bd, idesc, (i | kk) != 0);
+                    const uint64_t bd = smem_desc(sbb + kk * 2 * 4096, 1024, 4096);
+#pragma unroll
+                    for (int h = 0; h < kAcc; ++h) {
+                        // Rows 128 h .. 128 h + 127 of the x tile (16 KB apart) into accumulator h.
+                        const uint64_t ad = smem_desc(sa + h * 16384 + kk * 32, 16, 1024);
+                        umma_f16(tmem + 256 * h, ad, bd, idesc, (i | kk) != 0);
+                    }
                 }
-                umma_commit(empty(s));
+                umma_commit(empty_b(sb));
+                umma_commit(empty_load(i % kLoadStages));
             }
             umma_commit(acc_full);
         }
@@ -266,20 +286,34 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         // Dequantization: warp dw handles packed tile column d = dw / 2, chunks {2 hc, 2 hc + 1} x 32.
         const int dw = warp - 2, d = dw >> 1, hc = dw & 1;
         const int cc = (lane >> 1) & 7;  // column group of every chunk this lane takes
+        // Byte offsets of the lane's 8 output chunks in a B stage (K row r = 8 ga + 4 (lane & 1) + wi).
+        uint32_t st_off[2][4];
+#pragma unroll
+        for (int r2 = 0; r2 < 2; ++r2) {
+            const int ga = (lane >> 4) + 2 * (2 * hc + r2);
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+                const int rr = 4 * (lane & 1) + wi;
+                st_off[r2][wi] = ga * 4096 + d * 1024 + rr * 128 + ((cc ^ rr) << 4);
+            }
+        }
+        const uint32_t ld_off = d * kPHalf + 16 * lane + 512 * (2 * hc);
         constexpr uint32_t kMagic = F16 ? 0x64006400u : 0x43004300u;
         constexpr uint32_t kMask = 0x000F000Fu;
         bool ok = true;
         for (int i = 0; i < num_k; ++i) {
-            const int s = i % kStages, u = i / kStages;
-            if (!mbar_wait(full_load(s), u & 1, abort)) {
+            const int sl = i % kLoadStages, ul = i / kLoadStages;
+            const int sb = i % kBStages, ub = i / kBStages;
+            if (!mbar_wait(full_load(sl), ul & 1, abort) || (ub > 0 && !mbar_wait(empty_b(sb), (ub - 1) & 1, abort))) {
                 ok = false;
                 break;
             }
-            const uint8_t *st = smem + s * kStageBytes;
-            const uint8_t *pk = st + kABytes + kBBytes + d * kPHalf;
+            const uint8_t *pk = smem + kPOff + sl * kPBytes + d * kPHalf;
+            const uint8_t *pw = smem + kPOff + sl * kPBytes + ld_off;
             // Scales and offset zeros of columns (p, p + 4) of the group, as 16-bit pairs.
             const uint4 sv = *reinterpret_cast<const uint4 *>(pk + 2048 + 16 * cc);
             const uint2 zv = *reinterpret_cast<const uint2 *>(pk + 2048 + 128 + 16 * cc);
+            const uint4 wv2[2] = {*reinterpret_cast<const uint4 *>(pw), *reinterpret_cast<const uint4 *>(pw + 512)};
             uint32_t sp[4], zp[4];
             {
                 const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};  // scale of column p at half p%2 of word p/2
@@ -296,46 +330,48 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                         s_pair = lo | (hi << 16);
                     }
                     sp[p] = s_pair;
-                    const uint32_t zlo = (p < 4 ? (zv.x >> (8 * p)) : 0) & 0xFFu;  // zero of column p
-                    const uint32_t zhi = (zv.y >> (8 * p)) & 0xFFu;                   // zero of column p + 4
-                    zp[p] = (kMagic & 0xFFFF0000u) | (kMagic & 0xFFFFu) | zlo | (zhi << 16);
+                    const uint32_t zlo = (zv.x >> (8 * p)) & 0xFFu;  // zero of column p
+                    const uint32_t zhi = (zv.y >> (8 * p)) & 0xFFu;  // zero of column p + 4
+                    zp[p] = kMagic | zlo | (zhi << 16);             // 128 + z (1024 + z) in both halves
                 }
             }
-            uint8_t *bt = smem + s * kStageBytes + kABytes;
+            uint8_t *bt = smem + kBOff + sb * kBBytes;
 #pragma unroll
             for (int r2 = 0; r2 < 2; ++r2) {
-                const int ic = lane + 32 * (2 * hc + r2);
-                const int ga = ic >> 4, b0 = 4 * (ic & 1);
-                const uint4 wv = *reinterpret_cast<const uint4 *>(pk + 16 * ic);
-                const uint32_t ws[4] = {wv.x, wv.y, wv.z, wv.w};
+                // Chunk lane + 32 (2 hc + r2) of the half tile: K rows 8 ga + 4 (lane & 1) .. +3, column group cc.
+                const uint32_t ws[4] = {wv2[r2].x, wv2[r2].y, wv2[r2].z, wv2[r2].w};
 #pragma unroll
                 for (int wi = 0; wi < 4; ++wi) {
                     const uint32_t w = ws[wi];
-                    const int r = ga * 8 + b0 + wi;  // K row within this 64-row step
                     uint4 o;
                     o.x = sub_mul2<F16>(and_or(w, kMask, kMagic), zp[0], sp[0]);        // columns 0, 4
                     o.y = sub_mul2<F16>(and_or(w >> 4, kMask, kMagic), zp[1], sp[1]);   // columns 1, 5
                     o.z = sub_mul2<F16>(and_or(w >> 8, kMask, kMagic), zp[2], sp[2]);   // columns 2, 6
                     o.w = sub_mul2<F16>(and_or(w >> 12, kMask, kMagic), zp[3], sp[3]);  // columns 3, 7
-                    const int rr = r & 7;
-                    *reinterpret_cast<uint4 *>(bt + (r >> 3) * 4096 + d * 1024 + rr * 128 + ((cc ^ rr) << 4)) = o;
+                    *reinterpret_cast<uint4 *>(bt + st_off[r2][wi]) = o;
                 }
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
-            if (lane == 0) mbar_arrive(full_mma(s));
+            if (lane == 0) {
+                mbar_arrive(full_b(sb));
+                mbar_arrive(empty_load(sl));
+            }
         }
 
-        // Epilogue: warp q = warp % 4 reads TMEM lanes 32q .. 32q + 31; warps 2-5 take accumulator
-        // columns 0-127, warps 6-9 columns 128-255.
-        const int q = warp & 3, ch = dw >> 2;
-        const int row = 32 * q + lane, tok = m0 + row;
+        // Epilogue: warp q = warp % 4 reads TMEM lanes 32q .. 32q + 31. With one accumulator, warps
+        // 2-5 take its columns 0-127 and warps 6-9 columns 128-255; with two, warps 2-5 take
+        // accumulator 0 (rows 0-127 of the tile) and warps 6-9 accumulator 1, all 256 columns.
+        const int q = warp & 3, half = dw >> 2;
+        const int acc = kAcc == 2 ? half : 0;
+        const int row = 128 * acc + 32 * q + lane, tok = m0 + row;
         if (ok && mbar_wait(acc_full, 0, abort)) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * q) << 16);
+            const uint32_t taddr = tmem + 256 * acc + (static_cast<uint32_t>(32 * q) << 16);
             // Column j = 8 cc + p' of a 64-wide block holds physical column 8 cc + perm[p'].
             constexpr int kPerm[8] = {0, 4, 1, 5, 2, 6, 3, 7};
             if constexpr (EPI == HMB_EPI_SWIGLU) {
+              for (int ch = kAcc == 2 ? 0 : half; ch < (kAcc == 2 ? 2 : half + 1); ++ch) {
                 // Block pair ch: gate = accumulator block 2 ch, up = block 2 ch + 1 (64 channels).
                 for (int hh = 0; hh < 2; ++hh) {
                     uint32_t gv[32], uv[32];
@@ -366,7 +402,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                         }
                     }
                 }
+              }
             } else {
+              for (int ch = kAcc == 2 ? 0 : half; ch < (kAcc == 2 ? 2 : half + 1); ++ch) {
                 for (int cb = 0; cb < 4; ++cb) {
                     uint32_t v[32];
                     tmem_ld32(taddr + 128 * ch + 32 * cb, v);
@@ -389,6 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                         }
                     }
                 }
+              }
             }
         }
     }
@@ -419,9 +458,10 @@ EncodeTiled encode_fn() {
     return fn;
 }
 
-template <bool F16, int EPI>
+template <int BM, bool F16, int EPI>
 int launch(const CUtensorMap &map, const GemmArgs &a, cudaStream_t stream) {
-    auto kernel = gemm_kernel<F16, EPI>;
+    auto kernel = gemm_kernel<BM, F16, EPI>;
+    constexpr int kSmemBytes = Plan<BM>::kSmemBytes;
     static std::mutex mu;
     static bool configured[64] = {};
     int dev = 0;
@@ -451,7 +491,7 @@ extern "C" {
 
 int hmb_w4a16_gemm_supports(int64_t m, int64_t k, int64_t n, int epilogue) {
     if (m <= 0 || k <= 0 || n <= 0 || k % kTileK) return 0;
-    return n % BN == 0 && (epilogue == HMB_EPI_STORE || epilogue == HMB_EPI_SWIGLU) && m <= (int64_t(1) << 31) / BM * BM;
+    return n % BN == 0 && (epilogue == HMB_EPI_STORE || epilogue == HMB_EPI_SWIGLU) && m < (int64_t(1) << 30);
 }
 
 int hmb_w4a16_gemm(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const void *x, int64_t ldx, int x_dtype, void *y,
@@ -475,7 +515,9 @@ int hmb_w4a16_gemm(const uint8_t *packed, int64_t packed_k, int64_t packed_n, co
     CUtensorMap map;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(k), static_cast<cuuint64_t>(m)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldx) * 2};
-    const cuuint32_t box[2] = {BK, BM};
+    // 256-row tiles (two accumulators per dequantized B tile) once there are more than 128 rows.
+    const int bm = m > 128 ? 256 : 128;
+    const cuuint32_t box[2] = {BK, static_cast<cuuint32_t>(bm)};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult cr = encode(&map, x_dtype == HMB_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                                const_cast<void *>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -495,10 +537,13 @@ int hmb_w4a16_gemm(const uint8_t *packed, int64_t packed_k, int64_t packed_n, co
     a.m = static_cast<int>(m);
     a.col_stride = (epilogue == HMB_EPI_SWIGLU && layout == HMB_GATE_UP_BLOCKED) ? a.n_tiles / 2 : 1;
     a.f16 = x_dtype == HMB_FP16;
-    if (x_dtype == HMB_FP16) {
-        return epilogue == HMB_EPI_SWIGLU ? launch<true, HMB_EPI_SWIGLU>(map, a, stream) : launch<true, HMB_EPI_STORE>(map, a, stream);
+    const bool swiglu = epilogue == HMB_EPI_SWIGLU;
+    if (bm == 256) {
+        if (x_dtype == HMB_FP16) return swiglu ? launch<256, true, HMB_EPI_SWIGLU>(map, a, stream) : launch<256, true, HMB_EPI_STORE>(map, a, stream);
+        return swiglu ? launch<256, false, HMB_EPI_SWIGLU>(map, a, stream) : launch<256, false, HMB_EPI_STORE>(map, a, stream);
     }
-    return epilogue == HMB_EPI_SWIGLU ? launch<false, HMB_EPI_SWIGLU>(map, a, stream) : launch<false, HMB_EPI_STORE>(map, a, stream);
+    if (x_dtype == HMB_FP16) return swiglu ? launch<128, true, HMB_EPI_SWIGLU>(map, a, stream) : launch<128, true, HMB_EPI_STORE>(map, a, stream);
+    return swiglu ? launch<128, false, HMB_EPI_SWIGLU>(map, a, stream) : launch<128, false, HMB_EPI_STORE>(map, a, stream);
 }
 
 int hmb_device_status(int *status, hmb_stream_t stream) {
