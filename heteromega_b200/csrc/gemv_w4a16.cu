@@ -528,3 +528,73 @@ int hmb_w4a16_gemv(const uint8_t *packed, int64_t packed_k, int64_t packed_n, co
 }
 
 }  // extern "C"
+
+// ---- the GEMV without caller workspace ------------------------------------------------------------------
+//
+// Some callers cannot hand this library a device allocation: a host runtime whose memory pool is owned
+// elsewhere and offers no scratch API, or a plugin ABI that only passes input and output buffers. For
+// them, hmb_w4a16_gemv_noalloc keeps the split-K scratch of the GEMV in a fixed array in device memory
+// that the library reserves when it is loaded, so a call allocates nothing.
+
+namespace hmb {
+namespace {
+
+constexpr size_t kStaticPartialBytes = 16u << 20;  // fp32 partial sums of column sets that cross warp chunks
+constexpr size_t kStaticScratchBytes = kCounterBytes + kStaticPartialBytes;
+
+// Every GPU that loads libhmb.so keeps this array until the process exits. In host code the name is a
+// stand-in, not a device address: only the pointer from cudaGetSymbolAddress may reach a kernel.
+static __device__ __align__(256) uint8_t g_gemv_scratch[kStaticScratchBytes];
+
+// Device address of g_gemv_scratch for the current device, looked up once per device.
+int static_scratch(uint8_t **out) {
+    static std::mutex mu;
+    static uint8_t *addr[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        set_cuda_error(e);
+        return HMB_ERR_CUDA;
+    }
+    if (dev >= 64) return HMB_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_gemv_scratch);
+        if (e != cudaSuccess) {
+            set_cuda_error(e);
+            return HMB_ERR_CUDA;
+        }
+        addr[dev] = static_cast<uint8_t *>(p);
+    }
+    *out = addr[dev];
+    return HMB_OK;
+}
+
+}  // namespace
+}  // namespace hmb
+
+extern "C" {
+
+int hmb_w4a16_gemv_noalloc(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const void *x, int64_t ldx, int x_dtype,
+                           void *y, int64_t ldy, int y_dtype, int64_t m, int64_t k, int64_t n, int64_t start_col, int epilogue,
+                           int layout, int split_k, hmb_stream_t stream) {
+    // The size check comes first, so an oversized call fails before touching the device.
+    const size_t need = hmb_w4a16_gemv_workspace(m, k, n, epilogue, split_k);
+    if (need == 0) return HMB_ERR_ARG;
+    if (need > hmb::kStaticScratchBytes) return HMB_ERR_WORKSPACE;
+    uint8_t *scratch = nullptr;
+    int rc = hmb::static_scratch(&scratch);
+    if (rc != HMB_OK) return rc;
+    // The counters must start at zero; a completed call leaves them so, but a call that failed on the
+    // device may not have.
+    const cudaError_t e = cudaMemsetAsync(scratch, 0, hmb::kCounterBytes, stream);
+    if (e != cudaSuccess) {
+        hmb::set_cuda_error(e);
+        return HMB_ERR_CUDA;
+    }
+    return hmb_w4a16_gemv(packed, packed_k, packed_n, x, ldx, x_dtype, y, ldy, y_dtype, m, k, n, start_col, epilogue, layout,
+                          split_k, scratch, hmb::kStaticScratchBytes, stream);
+}
+
+}  // extern "C"

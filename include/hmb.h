@@ -125,6 +125,20 @@ int hmb_w4a16_gemv(const uint8_t *packed, int64_t packed_k, int64_t packed_n, co
                    int split_k, void *workspace, size_t workspace_bytes, hmb_stream_t stream);
 size_t hmb_w4a16_gemv_workspace(int64_t m, int64_t k, int64_t n, int epilogue, int split_k);
 
+/* hmb_w4a16_gemv without a workspace argument, for callers that cannot allocate device memory (a host
+ * runtime that owns the device memory pool and exposes no scratch API, or a plugin ABI that hands over
+ * only input and output buffers). No counterpart in the reference: its kernels take scratch from the
+ * PyTorch caching allocator. The split-K scratch lives in a fixed 16 MiB + 64 KiB array in device
+ * memory that every GPU loading libhmb.so keeps until the process exits; a call that would need more
+ * (see hmb_w4a16_gemv_workspace) returns HMB_ERR_WORKSPACE before touching the device. The call
+ * itself allocates nothing. The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress), so make that first call before any stream capture. All calls share the one
+ * array: each clears its counters first, and calls whose kernels overlap on the GPU (different
+ * streams, or different host threads) race on it and give wrong results. */
+int hmb_w4a16_gemv_noalloc(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const void *x, int64_t ldx, int x_dtype,
+                           void *y, int64_t ldy, int y_dtype, int64_t m, int64_t k, int64_t n, int64_t start_col, int epilogue,
+                           int layout, int split_k, hmb_stream_t stream);
+
 /* Prefill GEMM on the tcgen05 tensor cores (TMA-fed, TMEM accumulator), same operands and epilogues
  * as hmb_w4a16_gemv: the weights are dequantized to bf16((q - z) * s) in shared memory, products
  * accumulate in fp32, the output rounds once. Needs n % 256 == 0 (HMB_ERR_UNSUPPORTED otherwise,
