@@ -48,7 +48,7 @@ class L2Flush:
         import torch
 
         self.buf = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=device)
-        self.out = torch.empty(1, dtype=torch.float32, device=device)
+        self.out = torch.empty((), dtype=torch.float32, device=device)
 
     def __call__(self):
         import torch
@@ -165,6 +165,12 @@ class ClockSampler:
 
 # ---- the product arm -----------------------------------------------------------------------------------
 
+def trace(*args):
+    """Progress lines on stderr when HMB_BENCH_TRACE=1 (debugging multi-rank runs)."""
+    if os.environ.get("HMB_BENCH_TRACE") == "1":
+        print(f"[bench rank {os.environ.get('RANK', '0')} {time.time():.3f}]", *args, file=sys.stderr, flush=True)
+
+
 def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -189,7 +195,7 @@ def run_hmb(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
     wl = workload(args)
     h, inter, L, m = wl["hidden"], wl["inter"], wl["layers"], wl["m"]
 
@@ -208,6 +214,7 @@ def run_hmb(args):
             layers.append(H.slice_packed_ffn(g, u, d, h, inter, 0, inter, H.GateUpLayout.kInterleaved))
         del g, u, d
     torch.cuda.synchronize()
+    trace("weights ready")
     stack = FfnStack(layers, h, dev, tp=tp)
     n_local = stack.layers[0].channels()
 
@@ -220,6 +227,7 @@ def run_hmb(args):
     use_graph = not args.no_graph
     if use_graph:
         graph, gx, gy = stack.graph(m)
+        trace("graph captured")
         gx.copy_(x_all)
         step = graph.replay
     else:
@@ -237,6 +245,7 @@ def run_hmb(args):
             flush()
         step()
     torch.cuda.synchronize()
+    trace("warm-up done")
 
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -258,12 +267,15 @@ def run_hmb(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         step_ms = float(t.item())
 
+    trace("timed steps done", step_ms)
     # Dominant kernel, timed alone: the fused gate/up + SiLU*up kernel of layer 0.
     w0 = stack.layers[0]
     dom = dominant_kernel(stack, w0, x_all[0], flush, stream, m)
 
+    trace("dominant kernel done")
     # End to end through the public API with host buffers (H2D of the step's inputs, D2H of its outputs).
     e2e = end_to_end(stack, x_all, m, args, flush, barrier, world, dev)
+    trace("e2e done")
 
     pk, pk_kind = peaks()
     from heteromega_b200.torch_ops import GEMV_MAX_ROWS
@@ -302,9 +314,13 @@ def run_hmb(args):
     }
     if rank == 0 and world == 1:
         line["cpu_baseline"] = cpu_baseline(wl, m, args.cpu_sample_s)
+    torch.cuda.synchronize()
+    if use_graph:
+        del graph, step
     stack.release()
     if world > 1:
         dist.barrier(device_ids=[local])
+        trace("destroying process group")
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -324,7 +340,7 @@ def dominant_kernel(stack, w, x, flush, stream, m, reps=20):
 
     launch()
     g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
+    with torch.cuda.graph(g, capture_error_mode="thread_local"):
         launch()
     big = flush if flush is not None else L2Flush(x.device)
     times = []

@@ -38,7 +38,7 @@ SIGNATURES = {
     "hmb_w4a16_gemv_workspace": (_sz, [_i64, _i64, _i64, _int, _int]),
     "hmb_w4a16_gemv_noalloc": (_int, [_vp, _i64, _i64, _vp, _i64, _int, _vp, _i64, _int, _i64, _i64, _i64, _i64, _int, _int,
                                       _int, _vp]),
-    "hmb_w4a16_gemm": (_int, [_vp, _i64, _i64, _vp, _i64, _int, _vp, _i64, _i64, _i64, _i64, _i64, _int, _int, _vp]),
+    "hmb_w4a16_gemm": (_int, [_vp, _i64, _i64, _vp, _i64, _int, _vp, _i64, _int, _i64, _i64, _i64, _i64, _int, _int, _vp]),
     "hmb_w4a16_gemm_supports": (_int, [_i64, _i64, _i64, _int]),
     "hmb_device_status": (_int, [_vp, _vp]),
     "hmb_silu_mul": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _int, _vp]),

@@ -67,7 +67,8 @@ struct GemmArgs {
     int n_tiles;     // tile columns computed (multiple of 4)
     int m;
     int col_stride;  // SwiGLU blocked layout: tile columns from gate to up; 1 = interleaved
-    int f16;         // activations and output are fp16 (else bf16)
+    int f16;         // activations (and a 16-bit output) are fp16, else bf16
+    int y_f32;       // HMB_EPI_STORE: write the fp32 sums instead of rounding them
 };
 
 // ---- PTX wrappers ----------------------------------------------------------------------------------
@@ -408,7 +409,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 for (int cb = 0; cb < 4; ++cb) {
                     uint32_t v[32];
                     tmem_ld32(taddr + 128 * ch + 32 * cb, v);
-                    if (tok < a.m) {
+                    if (tok < a.m && a.y_f32) {
+                        float *y = static_cast<float *>(a.y) + static_cast<int64_t>(tok) * a.ldy + nb * BN + 128 * ch + 32 * cb;
+#pragma unroll
+                        for (int g8 = 0; g8 < 4; ++g8) {
+                            float o[8];
+#pragma unroll
+                            for (int t = 0; t < 8; ++t) o[kPerm[t]] = __uint_as_float(v[8 * g8 + t]);
+                            *reinterpret_cast<float4 *>(y + 8 * g8) = make_float4(o[0], o[1], o[2], o[3]);
+                            *reinterpret_cast<float4 *>(y + 8 * g8 + 4) = make_float4(o[4], o[5], o[6], o[7]);
+                        }
+                    } else if (tok < a.m) {
                         uint16_t *y = static_cast<uint16_t *>(a.y) + static_cast<int64_t>(tok) * a.ldy + nb * BN + 128 * ch + 32 * cb;
 #pragma unroll
                         for (int g8 = 0; g8 < 4; ++g8) {
@@ -495,7 +506,7 @@ int hmb_w4a16_gemm_supports(int64_t m, int64_t k, int64_t n, int epilogue) {
 }
 
 int hmb_w4a16_gemm(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const void *x, int64_t ldx, int x_dtype, void *y,
-                   int64_t ldy, int64_t m, int64_t k, int64_t n, int64_t start_col, int epilogue, int layout,
+                   int64_t ldy, int y_dtype, int64_t m, int64_t k, int64_t n, int64_t start_col, int epilogue, int layout,
                    hmb_stream_t stream) {
     if (!packed || !x || !y || m <= 0) return HMB_ERR_ARG;
     if (k <= 0 || n <= 0 || k % kTileK || n % kTileN || packed_k % kTileK || packed_n % kTileN || start_col < 0 ||
@@ -503,6 +514,7 @@ int hmb_w4a16_gemm(const uint8_t *packed, int64_t packed_k, int64_t packed_n, co
         return HMB_ERR_ARG;
     if (x_dtype != HMB_BF16 && x_dtype != HMB_FP16) return HMB_ERR_ARG;
     if (epilogue != HMB_EPI_STORE && epilogue != HMB_EPI_SWIGLU) return HMB_ERR_ARG;
+    if (y_dtype != x_dtype && !(y_dtype == HMB_FP32 && epilogue == HMB_EPI_STORE)) return HMB_ERR_ARG;
     if (epilogue == HMB_EPI_SWIGLU && layout != HMB_GATE_UP_BLOCKED && layout != HMB_GATE_UP_INTERLEAVED) return HMB_ERR_ARG;
     if (!hmb_w4a16_gemm_supports(m, k, n, epilogue)) return HMB_ERR_UNSUPPORTED;
     if (epilogue == HMB_EPI_SWIGLU && layout == HMB_GATE_UP_BLOCKED && (n / 2) % (2 * kTileN)) return HMB_ERR_UNSUPPORTED;
@@ -537,6 +549,7 @@ int hmb_w4a16_gemm(const uint8_t *packed, int64_t packed_k, int64_t packed_n, co
     a.m = static_cast<int>(m);
     a.col_stride = (epilogue == HMB_EPI_SWIGLU && layout == HMB_GATE_UP_BLOCKED) ? a.n_tiles / 2 : 1;
     a.f16 = x_dtype == HMB_FP16;
+    a.y_f32 = y_dtype == HMB_FP32;
     const bool swiglu = epilogue == HMB_EPI_SWIGLU;
     if (bm == 256) {
         if (x_dtype == HMB_FP16) return swiglu ? launch<256, true, HMB_EPI_SWIGLU>(map, a, stream) : launch<256, true, HMB_EPI_STORE>(map, a, stream);

@@ -64,7 +64,8 @@ class FfnStack:
             torch.cuda.current_stream(self.device).wait_stream(s)
             torch.cuda.synchronize(self.device)
             graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
+            # thread_local: NCCL's watchdog thread keeps querying its events while this thread captures.
+            with torch.cuda.graph(graph, capture_error_mode="thread_local"):
                 self.forward(x_all, y_all, scratch)
             g = (graph, x_all, y_all, scratch)
             self._graphs[m] = g
@@ -84,6 +85,11 @@ class FfnStack:
         return 2 * len(self.layers)
 
     def release(self):
+        """Free the captured graphs. With a process group this must precede destroy_process_group: a
+        live graph that holds an NCCL call keeps the communicator from shutting down. reset() frees
+        the executable graph even where a caller still holds a reference to the CUDAGraph object."""
+        for g in self._graphs.values():
+            g[0].reset()
         self._graphs.clear()
 
 

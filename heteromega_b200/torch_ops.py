@@ -102,14 +102,15 @@ def _w4a16_gemm(out, x, packed, k, n, packed_k, packed_n, start_col, epilogue, l
     m = x.shape[0]
     if out.shape[0] != m:
         raise ValueError("w4a16_gemm: x and out must have the same number of rows")
-    if out.dtype != x.dtype:
-        raise ValueError("w4a16_gemm: out must have the activation dtype")
+    if out.dtype != x.dtype and not (out.dtype == torch.float32 and epilogue == _lib.HMB_EPI_STORE):
+        raise ValueError("w4a16_gemm: out must have the activation dtype (or fp32 without an epilogue)")
     if packed.dtype != torch.uint8 or not packed.is_contiguous():
         raise ValueError("w4a16_gemm: packed must be contiguous uint8")
     if packed.numel() != lib().hmb_packed_bytes(packed_k, packed_n):
         raise ValueError(f"w4a16_gemm: packed has {packed.numel()} bytes, not those of [{packed_k}, {packed_n}]")
     check(lib().hmb_w4a16_gemm(packed.data_ptr(), packed_k, packed_n, x.data_ptr(), x.stride(0), _dtype_code(x),
-                               out.data_ptr(), out.stride(0), m, k, n, start_col, epilogue, layout, _stream(x)), "w4a16_gemm")
+                               out.data_ptr(), out.stride(0), _dtype_code(out), m, k, n, start_col, epilogue, layout,
+                               _stream(x)), "w4a16_gemm")
 
 
 def gemm_supported(m, k, n, epilogue):
@@ -124,7 +125,7 @@ def w4a16_linear(out, x, packed, k, n, packed_k, packed_n, start_col=0, epilogue
     """The product's packed matmul: the decode GEMV for m <= GEMV_MAX_ROWS, the tcgen05 GEMM above it
     when the shape allows, else the GEMV over row chunks."""
     m = x.shape[0] if x.dim() == 2 else 1
-    if m > GEMV_MAX_ROWS and out.dtype == x.dtype and gemm_supported(m, k, n, epilogue):
+    if m > GEMV_MAX_ROWS and gemm_supported(m, k, n, epilogue):
         ops.w4a16_gemm(out, x, packed, k, n, packed_k, packed_n, start_col, epilogue, layout)
     else:
         ops.w4a16_gemv(out, x, packed, k, n, packed_k, packed_n, start_col, epilogue, layout, split_k)

@@ -140,13 +140,13 @@ int hmb_w4a16_gemv_noalloc(const uint8_t *packed, int64_t packed_k, int64_t pack
                            int layout, int split_k, hmb_stream_t stream);
 
 /* Prefill GEMM on the tcgen05 tensor cores (TMA-fed, TMEM accumulator), same operands and epilogues
- * as hmb_w4a16_gemv: the weights are dequantized to bf16((q - z) * s) in shared memory, products
+ * as hmb_w4a16_gemv (y_dtype: x_dtype, or HMB_FP32 for HMB_EPI_STORE): the weights are dequantized to bf16((q - z) * s) in shared memory, products
  * accumulate in fp32, the output rounds once. Needs n % 256 == 0 (HMB_ERR_UNSUPPORTED otherwise,
  * see hmb_w4a16_gemm_supports); any m. Replaces hipkernels::w4a16_gemm_fused_packed and
  * w4a16_gemm_fused_packed_tiles with fuse_activation (include/hipkernels/w4a16_gemm_packed.hpp:38-48) and
  * heteromega::gemm_w4a16 (gpu_ffn.hpp:101-107). */
 int hmb_w4a16_gemm(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const void *x, int64_t ldx, int x_dtype, void *y,
-                   int64_t ldy, int64_t m, int64_t k, int64_t n, int64_t start_col, int epilogue, int layout,
+                   int64_t ldy, int y_dtype, int64_t m, int64_t k, int64_t n, int64_t start_col, int epilogue, int layout,
                    hmb_stream_t stream);
 int hmb_w4a16_gemm_supports(int64_t m, int64_t k, int64_t n, int epilogue);
 

@@ -86,6 +86,22 @@ def test_gemm_fp16_activations(cuda, oracle):
     assert_close(y.float().cpu().numpy(), x.astype(np.float64) @ w, LEVEL, "fp16 gemm")
 
 
+def test_gemm_fp32_output(cuda, oracle):
+    """Unrounded fp32 sums (the tensor-parallel partials): within the bf16-weight error of the oracle."""
+    k, n, m = 4096, 512, 200
+    p = rand_matrix(oracle, k, n, seed=61)
+    x = oracle.bf16_bits(np.random.default_rng(62).standard_normal((m, k)))
+    y32, _ = oracle.gemv(p, k, n, x)
+    y = torch.empty(m, n, dtype=torch.float32, device=cuda)
+    ops.w4a16_gemm(y, dev16(x, cuda), torch.from_numpy(p).to(cuda), k, n, k, n, 0, 0, 0)
+    yb = torch.empty(m, n, dtype=torch.bfloat16, device=cuda)
+    ops.w4a16_gemm(yb, dev16(x, cuda), torch.from_numpy(p).to(cuda), k, n, k, n, 0, 0, 0)
+    torch.cuda.synchronize()
+    assert_close(y.cpu().numpy(), y32, LEVEL, "gemm fp32 out")
+    # the bf16 output is the fp32 one rounded
+    assert torch.equal(y.to(torch.bfloat16), yb)
+
+
 def test_gemm_rejects_unsupported_width(cuda, oracle):
     p = torch.zeros(H.gpu_ffn.packed_bytes(128, 192), dtype=torch.uint8, device=cuda)
     x = torch.zeros(32, 128, dtype=torch.bfloat16, device=cuda)

@@ -1,0 +1,149 @@
+"""Tensor-parallel FFN: the channel partition across ranks and the per-layer boundary all-reduce.
+
+CPU part (gloo, world size 2): each rank slices its shard out of the whole packed layer with the host
+slice path, computes its partial output with the CPU oracle, and the all-reduce of the partials must
+give the unsharded FFN — the algebra of npu/ffn/reference.py:200-221 over P ranks. Also checks the
+partition planner against the reference's from_ratio rounding.
+GPU part (NCCL, 2 GPUs): the same through the CUDA kernels; skipped with fewer GPUs.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import heteromega_b200 as H
+from heteromega_b200.partition import DeviceModel, FFNPartition, best_ratios, plan_shards, predict_layer_time
+from heteromega_b200.tensor_parallel import TensorParallelFfn
+from heteromega_b200.weights import synthetic_layer
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_from_ratio_matches_reference(golden):
+    for inter, ratio, npu in golden("contract")["from_ratio"]:
+        assert FFNPartition.from_ratio(int(inter), float(ratio)).npu_channels == int(npu)
+    with pytest.raises(ValueError):
+        FFNPartition.from_ratio(14336, 1.5)
+    with pytest.raises(ValueError):
+        FFNPartition(14336, 100)
+
+
+@pytest.mark.parametrize("inter,world", [(8192, 2), (14336, 8), (13824, 8), (28672, 8), (13824, 3), (1024, 8)])
+def test_plan_shards_cover_and_align(inter, world):
+    shares = plan_shards(inter, world)
+    assert shares[0][0] == 0 and shares[-1][1] == inter
+    for (b, e), (b2, _) in zip(shares, shares[1:]):
+        assert e == b2
+    for b, e in shares:
+        assert e > b and b % 128 == 0 and e % 128 == 0
+    sizes = [e - b for b, e in shares]
+    assert max(sizes) - min(sizes) <= 128
+    if inter == 13824 and world == 8:
+        assert sorted(set(sizes)) == [1664, 1792] and sizes.count(1792) == 4
+
+
+def test_cost_model_prefers_balanced_shares():
+    dev = DeviceModel(hbm_gbs=6457.0, tflops=1677.0, overhead_us=2.0)
+    ratios, shares = best_ratios(8192, 28672, 1, [dev] * 4, allreduce_us=5.0)
+    assert [e - b for b, e in shares] == [7168] * 4
+    t1 = predict_layer_time(8192, [(0, 28672)], 1, [dev])
+    t4 = predict_layer_time(8192, shares, 1, [dev] * 4, allreduce_us=5.0)
+    assert t4 < t1
+
+
+def _gloo_rank(rank, world, port, hidden, inter, m, out_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import sys
+
+        sys.path.insert(0, REPO)
+        from oracle import oracle as O
+
+        layer = synthetic_layer(hidden, inter, layer=3)
+        g = H.pack_w4a16(layer.gate_q, layer.gate_s, layer.gate_z)
+        u = H.pack_w4a16(layer.up_q, layer.up_s, layer.up_z)
+        d = H.pack_w4a16(layer.down_q, layer.down_s, layer.down_z)
+        tp = TensorParallelFfn(hidden, inter)
+        tp.add_layer(g, u, d)  # host slice path: CPU tensors
+        w = tp.layers[0]
+        x = O.bf16_bits(np.random.default_rng(5).standard_normal((m, hidden)))
+        _, part = O.ffn(w.gate_up.numpy(), w.down.numpy(), hidden, w.channels(), w.stored_channels(), int(w.layout), x)
+        partial = torch.from_numpy(np.ascontiguousarray(part))
+        tp.reduce_partials(partial)
+        if rank == 0:
+            full = H.pack_ffn_slice(layer, 0, inter, H.GateUpLayout.kInterleaved)
+            _, ref = O.ffn(full.gate_up.numpy(), full.down.numpy(), hidden, inter, inter, 1, x)
+            np.savez(out_path, got=partial.numpy(), ref=ref, shares=np.array(tp.shares))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("inter", [1024, 1152])
+def test_gloo_partials_sum_to_full_ffn(tmp_path, inter):
+    hidden, m, world = 256, 3, 2
+    out = str(tmp_path / "tp.npz")
+    mp.start_processes(_gloo_rank, args=(world, free_port(), hidden, inter, m, out), nprocs=world, join=True,
+                       start_method="spawn")
+    r = np.load(out)
+    assert len(r["shares"]) == world
+    from metrics import assert_close
+
+    assert_close(r["got"], r["ref"], (1e-5, 1e-5, 0.9999999), "sum of rank partials")
+
+
+def _nccl_rank(rank, world, port, out_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        from heteromega_b200.weights import synthetic_packed_device
+
+        hidden, inter = 2048, 8192
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(11)
+        g = synthetic_packed_device(hidden, inter, dev, gen)
+        u = synthetic_packed_device(hidden, inter, dev, gen)
+        d = synthetic_packed_device(inter, hidden, dev, gen)
+        tp = TensorParallelFfn(hidden, inter)
+        tp.add_layer(g, u, d)
+        full = H.slice_packed_ffn(g, u, d, hidden, inter, 0, inter, H.GateUpLayout.kInterleaved)
+        res = {}
+        for m in (1, 300):
+            gen.manual_seed(12 + m)
+            x = torch.randn(m, hidden, device=dev, generator=gen).to(torch.bfloat16)
+            y = torch.empty(m, hidden, dtype=torch.bfloat16, device=dev)
+            tp.forward(0, x, y)
+            ref = torch.empty_like(y)
+            H.gpu_ffn_slice_forward(full, x, None, ref)
+            torch.cuda.synchronize()
+            res[f"got{m}"], res[f"ref{m}"] = y.float().cpu().numpy(), ref.float().cpu().numpy()
+        if rank == 0:
+            np.savez(out_path, **res)
+        dist.barrier(device_ids=[rank])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_nccl_two_gpus(tmp_path):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    out = str(tmp_path / "nccl.npz")
+    mp.start_processes(_nccl_rank, args=(2, free_port(), out), nprocs=2, join=True, start_method="spawn")
+    r = np.load(out)
+    from metrics import LEVEL, assert_close
+
+    for m in (1, 300):
+        assert_close(r[f"got{m}"], r[f"ref{m}"], LEVEL, f"TP2 vs single GPU m={m}")
