@@ -1,0 +1,410 @@
+// W4A16 prefill GEMM over CTA pairs (tcgen05.mma cta_group::2), persistent, sm_100a.
+//
+// Same contract and arithmetic as the one-CTA kernel (gemm_w4a16_tc.cu): weights dequantized to
+// bf16((q - z) * s) per 128-row group (src/hipkernels/w4a16_gemm_packed.cu:491-497), fp32
+// accumulation, one rounding of the output, optional SwiGLU epilogue.
+//
+// A cluster of two CTAs (two SMs) computes 256 x 256 output tiles: CTA r holds rows 128 r .. 128 r
+// + 127 of x and columns 128 r .. 128 r + 127 of the dequantized weights in its shared memory, and
+// rows 128 r .. 128 r + 127 of the fp32 result (all 256 columns) in its TMEM. The pair walks the
+// tiles round robin (tile = cluster + i * clusters; the larger operand stays in L2). Per CTA:
+//   warp 0      TMA of its 128 x 64 tile of x; the completion bytes of both CTAs count on the even
+//               CTA's barrier, which the even CTA arms with both tiles' bytes;
+//   warp 1      allocates 512 TMEM columns (two 256-column accumulators) for the pair; in the even
+//               CTA one thread issues tcgen05.mma M=256 N=256 K=16 for the pair and commits each
+//               stage to the barriers of both CTAs;
+//   warp 2      cp.async.bulk of the 64-row halves of its two packed tiles with scales and zeros;
+//   warps 3-10  dequantize into the B operand (MN-major, SWIZZLE_128B), then arrive on the even
+//               CTA's barrier; they form groups that work on successive K steps concurrently;
+//   warps 11-14 epilogue: tcgen05.ld of one accumulator while the other one is being computed,
+//               SwiGLU or plain store, then release the accumulator on the even CTA's barrier.
+// x, packed and B stages have separate rings, so a stage of packed weights is refilled as soon as
+// it is dequantized and a tile of x as soon as the MMA has read it.
+//
+// Every wait is bounded (one second); a wait that gives up records HMB_ERR_TIMEOUT in the status
+// word and the CTA winds down. Before leaving, each role waits (bounded) for the arrivals that
+// the peer CTA still owes it, so that no arrival targets a CTA that has exited.
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "gemm_internal.h"
+#include "tcgen05.cuh"
+
+namespace hmb {
+namespace {
+
+using namespace tc;
+
+constexpr int BK = 64;
+constexpr int kXBytes = 128 * BK * 2;  // this CTA's 128 rows of x for one K step
+constexpr int kPHalf = 2048 + 256;     // half a packed tile + its scales and zeros
+constexpr int kPBytes = 2 * kPHalf;    // this CTA's two tile columns
+constexpr int kBBytes = 128 * BK * 2;  // this CTA's 128 columns of the dequantized B
+#ifndef HMB_PAIR_DQ_GROUPS
+#define HMB_PAIR_DQ_GROUPS 4
+#endif
+// The dequant warps form kDqGroups groups that take successive K steps round robin: the latency of
+// one step (waits, shared loads, stores, proxy fence, arrivals) overlaps across groups instead of
+// bounding the step rate. A group can only start a step whose B stage the MMA has released, so the
+// B ring holds one stage per group plus the one the MMA is reading.
+constexpr int kDqGroups = HMB_PAIR_DQ_GROUPS;
+constexpr int kDequantWarps = 8, kEpiWarps = 4;
+constexpr int kDqWarpsPerGroup = kDequantWarps / kDqGroups;
+constexpr int kChunksPerWarp = 8 / kDqWarpsPerGroup;  // 512-byte chunks of the CTA's packed half tiles per step
+constexpr int kBStages = kDqGroups + 1, kAccStages = 2;
+constexpr int kXStages = kDqGroups >= 4 ? 6 : 7, kPStages = 8;
+static_assert(kDequantWarps % kDqGroups == 0 && kChunksPerWarp <= 4, "dequant groups");
+constexpr int kWarpX = 0, kWarpMma = 1, kWarpP = 2, kWarpDq0 = 3, kWarpEpi0 = kWarpDq0 + kDequantWarps;
+constexpr int kThreads = (kWarpEpi0 + kEpiWarps) * 32;
+constexpr int kXOff = 0;
+constexpr int kBOff = kXOff + kXStages * kXBytes;  // 1024-aligned stages (SWIZZLE_128B atoms)
+constexpr int kPOff = kBOff + kBStages * kBBytes;
+constexpr int kBarOff = kPOff + kPStages * kPBytes;
+constexpr int kNumBars = 2 * (kXStages + kPStages + kAccStages) + kBStages;
+static_assert(kXStages >= kBStages, "the done ring serves both the x and the B ring");
+constexpr int kSmemBytes = 1024 + kBarOff + 8 * kNumBars + 16;
+constexpr int kTmemCols = 256 * kAccStages;
+static_assert(kSmemBytes <= 227 * 1024, "shared memory plan");
+static_assert(kBOff % 1024 == 0 && kPOff % 1024 == 0, "stage alignment");
+
+template <bool F16, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const PairArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t bars = sbase + kBarOff;
+    // done(j % kXStages) completes when the pair MMA of K step j has finished reading its x and B
+    // stages (one commit per step; kXStages >= kBStages, so neither ring can lap it).
+    auto full_x = [&](int s) { return bars + 8 * s; };
+    auto done = [&](int s) { return bars + 8 * (kXStages + s); };
+    auto full_p = [&](int s) { return bars + 8 * (2 * kXStages + s); };
+    auto empty_p = [&](int s) { return bars + 8 * (2 * kXStages + kPStages + s); };
+    auto full_b = [&](int s) { return bars + 8 * (2 * kXStages + 2 * kPStages + s); };
+    auto tmem_full = [&](int s) { return bars + 8 * (2 * kXStages + 2 * kPStages + kBStages + s); };
+    auto tmem_empty = [&](int s) { return bars + 8 * (2 * kXStages + 2 * kPStages + kBStages + kAccStages + s); };
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + kBarOff + 8 * kNumBars);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int cluster = static_cast<int>(cluster_id_x()), nclusters = static_cast<int>(nclusters_x());
+    const int num_k = 2 * a.k_tiles;
+    // Tile t -> (row block, column block): the operand that is larger in bytes stays resident in L2
+    // while the other one streams (column blocks fastest when x is the larger one).
+    auto tile_mb = [&](int t) { return a.cols_fastest ? t / a.n_blocks : t % a.m_blocks; };
+    auto tile_nb = [&](int t) { return a.cols_fastest ? t % a.n_blocks : t / a.m_blocks; };
+
+    // Tile column d (0..3) of pair tile column nb, relative to the packed matrix. SwiGLU keeps them
+    // as [gate, up, gate, up] of two 64-channel blocks.
+    auto tile_col = [&](int nb, int d) {
+        if (EPI == HMB_EPI_SWIGLU && a.col_stride != 1) return a.col_tile0 + 2 * nb + (d >> 1) + (d & 1) * a.col_stride;
+        return a.col_tile0 + 4 * nb + d;
+    };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kXStages; ++s) {
+            mbar_init(full_x(s), 1);  // even CTA: its producer's arrive.expect_tx (both CTAs' bytes)
+            mbar_init(done(s), 1);    // the pair MMA's commit
+        }
+        for (int s = 0; s < kPStages; ++s) {
+            mbar_init(full_p(s), 1);
+            mbar_init(empty_p(s), kDqWarpsPerGroup);
+        }
+        for (int s = 0; s < kBStages; ++s) mbar_init(full_b(s), 2 * kDqWarpsPerGroup);  // even CTA: one dequant group of each CTA
+        for (int s = 0; s < kAccStages; ++s) {
+            mbar_init(tmem_full(s), 1);
+            mbar_init(tmem_empty(s), 2 * kEpiWarps);  // even CTA: epilogue warps of both CTAs
+        }
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == kWarpMma) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    fence_before_sync();
+    __syncthreads();
+    cluster_sync();  // the peer's barriers are initialised before anyone arrives on them
+    fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == kWarpX) {
+        if (lane == 0) {
+            prefetch_tensormap(&tmap_x);
+            int it = 0;
+            bool ok = true;
+            for (int tile = cluster; ok && tile < a.num_tiles; tile += nclusters) {
+                const int mb = tile_mb(tile);
+                const int row0 = 256 * mb + 128 * static_cast<int>(rank);
+                for (int i = 0; i < num_k; ++i, ++it) {
+                    const int s = it % kXStages, u = it / kXStages;
+                    if (u > 0 && !mbar_wait(done(s), (u - 1) & 1, abort, a.status)) {
+                        ok = false;
+                        break;
+                    }
+                    if (leader) mbar_expect_tx(full_x(s), 2 * kXBytes);
+                    tma_load_2d_pair(sbase + kXOff + s * kXBytes, &tmap_x, i * BK, row0, mapa(full_x(s), 0));
+                }
+            }
+            // The pair MMA's last commits to this CTA, one per barrier of the done ring (bounded).
+            for (int j = std::max(0, it - kXStages); j < it; ++j) mbar_wait(done(j % kXStages), (j / kXStages) & 1, abort, a.status);
+        }
+    } else if (warp == kWarpP) {
+        if (lane == 0) {
+            int it = 0;
+            bool ok = true;
+            for (int tile = cluster; ok && tile < a.num_tiles; tile += nclusters) {
+                const int nb = tile_nb(tile);
+                const uint8_t *col_base[2];
+                for (int d = 0; d < 2; ++d)
+                    col_base[d] = a.packed + tile_index(tile_col(nb, 2 * static_cast<int>(rank) + d), 0, a.tiles_k_total, a.tiles_n_total) * kTileBytes;
+                for (int i = 0; i < num_k; ++i, ++it) {
+                    const int s = it % kPStages, u = it / kPStages;
+                    if (u > 0 && !mbar_wait(empty_p(s), (u - 1) & 1, abort, a.status)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(full_p(s), kPBytes);
+                    const int kt = i >> 1, h = i & 1;
+                    for (int d = 0; d < 2; ++d) {
+                        const uint8_t *t = col_base[d] + static_cast<int64_t>(kt) * kTileBytes;
+                        const uint32_t pd = sbase + kPOff + s * kPBytes + d * kPHalf;
+                        bulk_load(pd, t + h * 2048, 2048, full_p(s));
+                        bulk_load(pd + 2048, t + 4096, 256, full_p(s));
+                    }
+                }
+            }
+            // Copies still in flight land before the CTA leaves (bounded).
+            for (int j = std::max(0, it - kPStages); j < it; ++j) mbar_wait(empty_p(j % kPStages), (j / kPStages) & 1, abort, a.status);
+        }
+    } else if (warp == kWarpMma) {
+        if (leader && lane == 0) {
+            constexpr uint32_t idesc = idesc_f16(F16, 256, 256);
+            // x: K-major, 128-byte rows, 8-row groups 1 KB apart. B: MN-major, two 64-column atoms
+            // 1 KB apart, 8-row K groups 2 KB apart. Per MMA (K = 16) x advances 32 bytes, B 4 KB.
+            const uint32_t a_lo0 = smem_desc_lo(sbase + kXOff, 16), b_lo0 = smem_desc_lo(sbase + kBOff, 1024);
+            constexpr uint32_t a_hi = smem_desc_hi(1024), b_hi = smem_desc_hi(2048);
+            int it = 0, t = 0;
+            bool ok = true;
+            for (int tile = cluster; ok && tile < a.num_tiles; tile += nclusters, ++t) {
+                const int acc = t % kAccStages, ua = t / kAccStages;
+                if (ua > 0 && !mbar_wait(tmem_empty(acc), (ua - 1) & 1, abort, a.status)) break;
+                fence_after_sync();
+                const uint32_t d = tmem + 256 * acc;
+                for (int i = 0; i < num_k; ++i, ++it) {
+                    const int sx = it % kXStages, sb = it % kBStages;
+                    // full_b implies full_x: the even CTA's dequant warps wait for both CTAs' x tiles
+                    // before they arrive.
+                    if (!mbar_wait(full_b(sb), (it / kBStages) & 1, abort, a.status)) {
+                        ok = false;
+                        break;
+                    }
+                    fence_after_sync();
+                    const uint32_t a_lo = a_lo0 + sx * (kXBytes >> 4), b_lo = b_lo0 + sb * (kBBytes >> 4);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        umma_f16_pair_lohi(d, a_lo + kk * 2, a_hi, b_lo + kk * 256, b_hi, idesc, (i | kk) != 0);
+                    umma_commit_pair(done(sx), 3);
+                }
+                if (ok) umma_commit_pair(tmem_full(acc), 3);
+            }
+            // The last releases of each accumulator by the epilogues of both CTAs (bounded).
+            for (int j = std::max(0, t - kAccStages); j < t; ++j) mbar_wait(tmem_empty(j % kAccStages), (j / kAccStages) & 1, abort, a.status);
+        }
+    } else if (warp < kWarpEpi0) {
+        // Dequantization: warp j belongs to group g = j / kDqWarpsPerGroup, which takes the K steps
+        // with it % kDqGroups == g, and handles kChunksPerWarp of the step's eight 512-byte chunks
+        // (chunk ch: tile column dl = ch / 4 of this CTA, quarter c = ch % 4 of its 64-row half tile).
+        // Lane L of chunk c takes the 16 bytes at 16 L: K rows 8 ga + 4 (L & 1) .. + 3
+        // (ga = 2 c + L / 16) of column group cc = (L / 2) % 8.
+        const int j = warp - kWarpDq0, g = j / kDqWarpsPerGroup, w = j % kDqWarpsPerGroup;
+        const int dl = (w * kChunksPerWarp) >> 2, c0 = (w * kChunksPerWarp) & 3;
+        const int cc = (lane >> 1) & 7;
+        uint32_t st_off[kChunksPerWarp][4];
+#pragma unroll
+        for (int r = 0; r < kChunksPerWarp; ++r) {
+            const int ga = 2 * (c0 + r) + (lane >> 4);
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+                const int rr = 4 * (lane & 1) + wi;
+                st_off[r][wi] = ga * 2048 + dl * 1024 + rr * 128 + ((cc ^ rr) << 4);
+            }
+        }
+        const uint32_t ld_off = dl * kPHalf + 16 * lane + 512 * c0;
+        int it = 0;
+        bool ok = true;
+        for (int tile = cluster; ok && tile < a.num_tiles; tile += nclusters) {
+            for (int i = 0; i < num_k; ++i, ++it) {
+                if (it % kDqGroups != g) continue;
+                const int s = it % kPStages, sb = it % kBStages, jb = it - kBStages;
+                if (!mbar_wait(full_p(s), (it / kPStages) & 1, abort, a.status) ||
+                    (jb >= 0 && !mbar_wait(done(jb % kXStages), (jb / kXStages) & 1, abort, a.status)) ||
+                    (leader && !mbar_wait(full_x(it % kXStages), (it / kXStages) & 1, abort, a.status))) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t *pk = smem + kPOff + s * kPBytes + dl * kPHalf;
+                uint32_t sp[4], zp[4];
+                group_consts<F16>(pk + 2048, pk + 2048 + 128, cc, sp, zp);
+                uint4 wv[kChunksPerWarp];
+#pragma unroll
+                for (int r = 0; r < kChunksPerWarp; ++r) wv[r] = *reinterpret_cast<const uint4 *>(smem + kPOff + s * kPBytes + ld_off + 512 * r);
+                uint8_t *bt = smem + kBOff + sb * kBBytes;
+#pragma unroll
+                for (int r = 0; r < kChunksPerWarp; ++r) {
+                    *reinterpret_cast<uint4 *>(bt + st_off[r][0]) = dequant_word<F16>(wv[r].x, sp, zp);
+                    *reinterpret_cast<uint4 *>(bt + st_off[r][1]) = dequant_word<F16>(wv[r].y, sp, zp);
+                    *reinterpret_cast<uint4 *>(bt + st_off[r][2]) = dequant_word<F16>(wv[r].z, sp, zp);
+                    *reinterpret_cast<uint4 *>(bt + st_off[r][3]) = dequant_word<F16>(wv[r].w, sp, zp);
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive_cluster(mapa(full_b(sb), 0));
+                    mbar_arrive(empty_p(s));
+                }
+            }
+        }
+    } else {
+        // Epilogue: warp q = warp % 4 reads TMEM lanes 32 q .. 32 q + 31 (rows of this CTA).
+        const int q = warp & 3;
+        int t = 0;
+        for (int tile = cluster; tile < a.num_tiles; tile += nclusters, ++t) {
+            const int acc = t % kAccStages;
+            if (!mbar_wait(tmem_full(acc), (t / kAccStages) & 1, abort, a.status)) break;
+            fence_after_sync();
+            const int mb = tile_mb(tile), nb = tile_nb(tile);
+            const int tok = 256 * mb + 128 * static_cast<int>(rank) + 32 * q + lane;
+            const uint32_t taddr = tmem + 256 * acc + (static_cast<uint32_t>(32 * q) << 16);
+            if constexpr (EPI == HMB_EPI_SWIGLU) {
+                for (int ch = 0; ch < 2; ++ch) {
+                    // Block pair ch: gate = columns 128 ch .. + 63, up = 128 ch + 64 .. + 127.
+                    for (int hh = 0; hh < 2; ++hh) {
+                        uint32_t gv[32], uv[32];
+                        tmem_ld32_nowait(taddr + 128 * ch + 32 * hh, gv);
+                        tmem_ld32_nowait(taddr + 128 * ch + 64 + 32 * hh, uv);
+                        tmem_wait_ld();
+                        if (tok < a.m) {
+                            uint16_t *y = static_cast<uint16_t *>(a.y) + static_cast<int64_t>(tok) * a.ldy + (2 * nb + ch) * kTileN + 32 * hh;
+#pragma unroll
+                            for (int g8 = 0; g8 < 4; ++g8) {
+                                uint32_t o[4];
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    uint32_t pr = 0;
+#pragma unroll
+                                    for (int hl = 0; hl < 2; ++hl) {
+                                        const int pp = perm_pos(2 * e + hl);
+                                        const float g = round16<F16>(__uint_as_float(gv[8 * g8 + pp]));
+                                        const float uu = round16<F16>(__uint_as_float(uv[8 * g8 + pp]));
+                                        pr |= to16<F16>(g / (1.0f + __expf(-g)) * uu) << (16 * hl);
+                                    }
+                                    o[e] = pr;
+                                }
+                                *reinterpret_cast<uint4 *>(y + 8 * g8) = make_uint4(o[0], o[1], o[2], o[3]);
+                            }
+                        }
+                    }
+                }
+            } else {
+                for (int cb = 0; cb < 8; ++cb) {
+                    uint32_t v[32];
+                    tmem_ld32(taddr + 32 * cb, v);
+                    if (tok < a.m && a.y_f32) {
+                        float *y = static_cast<float *>(a.y) + static_cast<int64_t>(tok) * a.ldy + nb * 256 + 32 * cb;
+#pragma unroll
+                        for (int g8 = 0; g8 < 4; ++g8) {
+                            float o[8];
+#pragma unroll
+                            for (int p = 0; p < 8; ++p) o[p] = __uint_as_float(v[8 * g8 + perm_pos(p)]);
+                            *reinterpret_cast<float4 *>(y + 8 * g8) = make_float4(o[0], o[1], o[2], o[3]);
+                            *reinterpret_cast<float4 *>(y + 8 * g8 + 4) = make_float4(o[4], o[5], o[6], o[7]);
+                        }
+                    } else if (tok < a.m) {
+                        uint16_t *y = static_cast<uint16_t *>(a.y) + static_cast<int64_t>(tok) * a.ldy + nb * 256 + 32 * cb;
+#pragma unroll
+                        for (int g8 = 0; g8 < 4; ++g8) {
+                            uint32_t o[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e)
+                                o[e] = to16<F16>(__uint_as_float(v[8 * g8 + perm_pos(2 * e)])) |
+                                       (to16<F16>(__uint_as_float(v[8 * g8 + perm_pos(2 * e + 1)])) << 16);
+                            *reinterpret_cast<uint4 *>(y + 8 * g8) = make_uint4(o[0], o[1], o[2], o[3]);
+                        }
+                    }
+                }
+            }
+            fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa(tmem_empty(acc), 0));
+        }
+    }
+
+    fence_before_sync();
+    __syncthreads();
+    cluster_sync();  // neither CTA leaves while the other may still address its shared memory or TMEM
+    if (warp == kWarpMma) {
+        fence_after_sync();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
+template <bool F16, int EPI>
+int launch(const CUtensorMap &map, const PairArgs &a, cudaStream_t stream) {
+    auto kernel = gemm_pair_kernel<F16, EPI>;
+    static std::mutex mu;
+    static int max_clusters[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 64) return HMB_ERR_UNSUPPORTED;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (max_clusters[dev] == 0) {
+            cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+            int n = 0;
+            if (e == cudaSuccess) {
+                cfg.gridDim = dim3(2 * sm_count());
+                e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+            }
+            if (e != cudaSuccess || n <= 0) {
+                set_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidConfiguration);
+                return HMB_ERR_CUDA;
+            }
+            max_clusters[dev] = n;
+        }
+    }
+    const int clusters = std::min(a.num_tiles, max_clusters[dev]);
+    cfg.gridDim = dim3(2 * clusters);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, map, a);
+    if (e != cudaSuccess) {
+        set_cuda_error(e);
+        return HMB_ERR_CUDA;
+    }
+    return launch_status();
+}
+
+}  // namespace
+
+int launch_gemm_pair(const CUtensorMap &map, const PairArgs &a, bool f16, int epilogue, cudaStream_t stream) {
+    if (f16) return epilogue == HMB_EPI_SWIGLU ? launch<true, HMB_EPI_SWIGLU>(map, a, stream) : launch<true, HMB_EPI_STORE>(map, a, stream);
+    return epilogue == HMB_EPI_SWIGLU ? launch<false, HMB_EPI_SWIGLU>(map, a, stream) : launch<false, HMB_EPI_STORE>(map, a, stream);
+}
+
+}  // namespace hmb
