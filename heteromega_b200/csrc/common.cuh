@@ -32,6 +32,32 @@ inline bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintp
 // Streaming multiprocessors of the current device (cached per device).
 int sm_count();
 
+// Device address of the status word on the current device (cached per device; nullptr on error). A
+// kernel that gives up a bounded wait ORs 1 into it; hmb_device_status() reads and clears it.
+int *device_status_word();
+
+// Programmatic dependent launch. A kernel launched with launch_pdl() may start while the previous
+// kernel of the stream is still running: it reads only its constant weights before pdl_wait(),
+// which returns once the previous kernel has completed and its writes are visible (at once when
+// there is no such kernel). pdl_launch_dependents() lets the next kernel start early.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename Kernel, typename... Args>
+cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // Position of tile (c, r) in a packed tiles_k x tiles_n matrix: tiles ordered by column modulo 8,
 // then column, then row.
 __host__ __device__ inline int64_t tile_index(int64_t c, int64_t r, int64_t tiles_k, int64_t tiles_n) {

@@ -51,7 +51,7 @@ constexpr int kTmemCols = 256;
 constexpr int kSmemBytes = 1024 + kBarOff + 256;
 static_assert(kBOff % 1024 == 0, "stage alignment");
 
-// Set to 1 by a kernel that gave up a bounded wait; read and cleared by hmb_device_status().
+// Set to 1 by a kernel (GEMM or GEMV) that gave up a bounded wait; read and cleared by hmb_device_status().
 __device__ int g_gemm_status = 0;
 
 struct GemmArgs {
@@ -304,21 +304,6 @@ EncodeTiled encode_fn() {
     return fn;
 }
 
-// Device address of g_gemm_status on the current device (cached per device).
-int *status_ptr() {
-    static std::mutex mu;
-    static int *addr[64] = {};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return nullptr;
-    std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
-        void *p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_gemm_status) != cudaSuccess) return nullptr;
-        addr[dev] = static_cast<int *>(p);
-    }
-    return addr[dev];
-}
-
 template <bool F16, int EPI>
 int launch(const CUtensorMap &map, const GemmArgs &a, cudaStream_t stream) {
     auto kernel = gemm_kernel<F16, EPI>;
@@ -343,6 +328,21 @@ int launch(const CUtensorMap &map, const GemmArgs &a, cudaStream_t stream) {
 }
 
 }  // namespace
+
+int *device_status_word() {
+    static std::mutex mu;
+    static int *addr[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_gemm_status) != cudaSuccess) return nullptr;
+        addr[dev] = static_cast<int *>(p);
+    }
+    return addr[dev];
+}
+
 }  // namespace hmb
 
 using namespace hmb;
@@ -372,7 +372,7 @@ int hmb_w4a16_gemm(const uint8_t *packed, int64_t packed_k, int64_t packed_n, co
     if (!aligned(packed, 16) || !aligned(x, 16) || !aligned(y, 16) || ldx % 8 || ldy % 8) return HMB_ERR_ALIGN;
 
     EncodeTiled encode = encode_fn();
-    int *status = status_ptr();
+    int *status = device_status_word();
     if (!encode || !status) return HMB_ERR_CUDA;
     // Both kernels load x in 64 x 128 boxes: the one-CTA kernel its 128-row tile, each CTA of a pair
     // its half of a 256-row tile.

@@ -8,9 +8,13 @@
 //   * Work is the stream of packed tiles. The tiles of a "column set" (one tile column, or the gate
 //     and up tile columns of 64 channels for the SwiGLU epilogue) form consecutive items, and the
 //     whole item range is cut into equal contiguous chunks, one per warp of a grid of one CTA per
-//     SM. Every warp streams its chunk through a private 5-stage ring of 16-byte cp.async copies
-//     in shared memory (4 tiles in flight per warp, ~128 KB per SM), so a small matrix is requested
-//     from HBM at once and a large one keeps the memory system full.
+//     SM. Every warp streams its chunk through a private ring in shared memory: each tile arrives
+//     as one 4352-byte cp.async.bulk (the tensor-memory-access engine, not per-lane requests) on a
+//     per-stage mbarrier, and the tile's rows of x as 16-byte cp.async copies. A small matrix is
+//     requested from HBM at once and a large one keeps the memory system full.
+//   * The kernel is launched as a programmatic dependent of the previous kernel in the stream: it
+//     requests its first weight tiles before waiting for that kernel (weights are constant), so
+//     the launch and the first HBM round trip overlap the previous kernel's tail.
 //   * The weights go through the tensor cores as exact integers. A nibble q becomes the bf16
 //     (fp16) number 128 + q (1024 + q) by OR-ing it into the mantissa of 0x4300 (0x6400), so one
 //     PRMT and two LOP3 turn 4 bytes into MMA operand registers. The MMA multiplies them with x and
@@ -24,8 +28,8 @@
 //     block b.
 //   * A column set that lies inside one warp's chunk is finished from that warp's registers. One
 //     that crosses chunks is finished by the last warp to contribute (an atomic counter per column
-//     set): it adds the fp32 partials of all contributors in chunk order, so results do not depend
-//     on timing.
+//     set): every contributor stores the fp32 sums of its valid rows, and the last one adds them in
+//     chunk order with all lanes (batches of loads in flight), so results do not depend on timing.
 //   * The SwiGLU epilogue writes bf16(SiLU(g) * u) from the bf16-rounded gate and up sums of the
 //     same lane, so gate/up never reach HBM.
 #include <algorithm>
@@ -36,10 +40,11 @@
 namespace hmb {
 namespace {
 
-constexpr int kSmemBudget = 224 * 1024;
+constexpr int kSmemBudget = 227 * 1024;
 constexpr int kXRowBytes = 288;  // 256 bytes of x per row and tile, padded so 4 rows hit distinct banks
 
-// Per-warp ring stage: [8 x 512 weight bytes, lane-major][128 scale bytes][128 zero bytes][m x 288 x bytes].
+// Per-warp ring stage: [the packed tile as stored: 4096 weight bytes, 128 scale bytes, 128 zero
+// bytes][m x 288 x bytes]. The ring's mbarriers follow all rings (8 bytes per warp and stage).
 __host__ __device__ constexpr int stage_bytes(int m) { return 4352 + kXRowBytes * m; }
 
 struct GemvArgs {
@@ -58,6 +63,7 @@ struct GemvArgs {
     int y_f32;
     int items;  // colsets * NCOL * k_tiles
     int warps;  // warps that share the items
+    int *status;  // device status word: 1 after a bounded wait gave up
 };
 
 template <bool F16>
@@ -81,6 +87,39 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst), "l"(src),
+                 "r"(bytes), "r"(bar)
+                 : "memory");
+}
+// Wait for phase `parity` of a ring barrier; false after one second (the warp then stops and the
+// status word reports HMB_ERR_TIMEOUT).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    uint64_t start = 0;
+    for (uint32_t i = 0;; ++i) {
+        uint32_t done;
+        asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                     : "=r"(done)
+                     : "r"(bar), "r"(parity)
+                     : "memory");
+        if (done) return true;
+        if ((i & 63) == 63) {
+            uint64_t now;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+            if (start == 0) {
+                start = now;
+            } else if (now - start > 1000000000ull) {
+                return false;
+            }
+        }
+    }
 }
 // Shared-memory loads as plain C++ accesses: ordered after cp.async.wait_group (its "memory" clobber)
 // and otherwise free for the compiler to schedule early. a is an offset from the dynamic smem base.
@@ -113,6 +152,7 @@ __device__ __forceinline__ void mma16816_zc(float (&d)[4], uint32_t a0, uint32_t
 }
 
 // Accumulates one staged tile into acc: acc += s * (sum (C+q) x - (C+z) sum x) for the lane's fragment.
+// wlane: offset of the lane's 16 bytes in each 512-byte weight chunk of the tile.
 // xrow[mt]: shared address of this lane's x row for token block mt (rows past m repeat row m-1; their
 // results are never stored).
 template <int MT, bool F16>
@@ -269,21 +309,19 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(const GemvArgs a) {
     // Stage addresses are offsets from g_smem for loads; cp.async takes the shared-window address.
     const uint32_t smem_base = static_cast<uint32_t>(__cvta_generic_to_shared(g_smem));
     const uint32_t ring = warp * S * sb;
-    // This lane's 16 bytes of weight chunk c are at tile + 512 c + lane_off: K rows 16c + 4t .. +3, column group g.
-    const int lane_off = 256 * (t >> 1) + 32 * g + 16 * (t & 1);
-    const uint32_t wlane = 16 * lane;
-    // Scales, zeros and x rows of a tile: 16 + 16 m copies of 16 bytes, taken by the lanes in turn.
-    // Lane copy r (r = 0, 1, ...) takes copy lane + 32 r.
-    const int meta = 16 + 16 * a.m;
-    // Per copy: destination offset in a stage, and for x rows the source offset from the tile's x.
-    int64_t meta_src[(16 + 16 * MAXM + 31) / 32];
-    uint32_t meta_dst[(16 + 16 * MAXM + 31) / 32];
+    // This lane's 16 bytes of weight chunk c are at tile + 512 c + wlane: K rows 16c + 4t .. +3, column group g.
+    const uint32_t wlane = 256 * (t >> 1) + 32 * g + 16 * (t & 1);
+    const uint32_t bars = smem_base + W * S * sb + warp * S * 8;  // this warp's ring barriers
+    // x rows of a tile: 16 m copies of 16 bytes, taken by the lanes in turn (copy lane + 32 r).
+    const int xcopies = 16 * a.m;
+    int64_t x_src[(16 * MAXM + 31) / 32];
+    uint32_t x_dst[(16 * MAXM + 31) / 32];
 #pragma unroll
-    for (int r = 0; r < (16 + 16 * MAXM + 31) / 32; ++r) {
+    for (int r = 0; r < (16 * MAXM + 31) / 32; ++r) {
         const int c = lane + 32 * r;
-        const int tok = (c - 16) >> 4, piece = (c - 16) & 15;
-        meta_dst[r] = c < 16 ? 4096 + c * 16 : 4352 + tok * kXRowBytes + piece * 16;
-        meta_src[r] = c < 16 ? 0 : (static_cast<int64_t>(tok) * a.ldx + piece * 8) * 2;
+        const int tok = c >> 4, piece = c & 15;
+        x_dst[r] = 4352 + tok * kXRowBytes + piece * 16;
+        x_src[r] = (static_cast<int64_t>(tok) * a.ldx + piece * 8) * 2;
     }
     uint32_t xrow[MT];
 #pragma unroll
@@ -295,35 +333,58 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(const GemvArgs a) {
     };
     Cursor in{b / per_set, (b % per_set) / a.k_tiles, b % a.k_tiles};
     const uint8_t *in_col = a.packed + tile_index(col_tile(in.j, in.s), 0, a.tiles_k_total, a.tiles_n_total) * kTileBytes;
-    uint32_t in_dst = ring + wlane;
-    const uint32_t ring_end = ring + S * sb;
-    auto issue = [&]() {
-        const uint8_t *tile = in_col + static_cast<int64_t>(in.kt) * kTileBytes;
-        const uint8_t *wsrc = tile + lane_off;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) cp_async16(smem_base + in_dst + c * 512, wsrc + 512 * c);
-        const uint32_t mdst = in_dst - wlane;
-        const uint8_t *xsrc = reinterpret_cast<const uint8_t *>(a.x + in.kt * kTileK);
-#pragma unroll
-        for (int r = 0; r < (16 + 16 * MAXM + 31) / 32; ++r) {
-            const int c = lane + 32 * r;
-            if (c < meta) {
-                const uint8_t *src = c < 16 ? tile + 4096 + c * 16 : xsrc + meta_src[r];
-                cp_async16(smem_base + mdst + meta_dst[r], src);
-            }
+    int in_stage = 0;
+    // The weight tile of the next item, as one bulk copy (lane 0) onto the stage's barrier.
+    auto issue_w = [&]() {
+        if (lane == 0) {
+            const uint32_t bar = bars + 8 * in_stage;
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // after this warp's reads of the stage
+            mbar_expect_tx(bar, kTileBytes);
+            bulk_load(smem_base + ring + in_stage * sb, in_col + static_cast<int64_t>(in.kt) * kTileBytes, kTileBytes, bar);
         }
+    };
+    // Its rows of x (cp.async, one commit group per tile), then advance to the next item.
+    auto issue_x = [&]() {
+        const uint8_t *xsrc = reinterpret_cast<const uint8_t *>(a.x + in.kt * kTileK);
+        const uint32_t dst = smem_base + ring + in_stage * sb;
+#pragma unroll
+        for (int r = 0; r < (16 * MAXM + 31) / 32; ++r)
+            if (lane + 32 * r < xcopies) cp_async16(dst + x_dst[r], xsrc + x_src[r]);
         const int j0 = in.j, s0 = in.s;
         in.next(a.k_tiles, NCOL);
         if (in.j != j0 || in.s != s0) {
             in_col = a.packed + tile_index(col_tile(in.j, in.s), 0, a.tiles_k_total, a.tiles_n_total) * kTileBytes;
         }
-        in_dst += sb;
-        if (in_dst >= ring_end) in_dst -= S * sb;
+        if (++in_stage == S) in_stage = 0;
     };
 
+    pdl_launch_dependents();
+    if (lane == 0) {
+        for (int q = 0; q < S; ++q) mbar_init(bars + 8 * q, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+    // Weights of the first S - 1 items before the previous kernel has finished; everything that
+    // kernel may write (x) or read (y, the workspace) only after pdl_wait().
+    {
+        const Cursor in0 = in;
+        const uint8_t *in_col0 = in_col;
+        for (int p = 0; p < S - 1; ++p) {
+            if (b + p < e) {
+                issue_w();
+                in.next(a.k_tiles, NCOL);
+                if (++in_stage == S) in_stage = 0;
+                in_col = a.packed + tile_index(col_tile(in.j, in.s), 0, a.tiles_k_total, a.tiles_n_total) * kTileBytes;
+            }
+        }
+        in = in0;
+        in_col = in_col0;
+        in_stage = 0;
+    }
+    pdl_wait();
 #pragma unroll
     for (int p = 0; p < S - 1; ++p) {
-        if (b + p < e) issue();
+        if (b + p < e) issue_x();
         cp_async_commit();
     }
 
@@ -341,13 +402,24 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(const GemvArgs a) {
             return;
         }
         const int c0 = chunk_of(first, a.items, a.warps), c1 = chunk_of(last, a.items, a.warps);
-        constexpr int kVals = MT * 16;
-        float *slot = a.partial + static_cast<int64_t>(gw + j) * (NCOL * kVals * 32);
+        // Contributor slot (one per warp and column set it shares): the valid rows only, as
+        // [slot s][token][64 columns] fp32, so small m moves little data.
+        constexpr int kSlot = NCOL * MT * 16 * 32;
+        float *slot = a.partial + static_cast<int64_t>(gw + j) * kSlot;
 #pragma unroll
-        for (int i = 0; i < kVals; ++i) {
-            __stcg(slot + i * 32 + lane, (&v0[0][0][0])[i]);
-            if (NCOL == 2) __stcg(slot + (kVals + i) * 32 + lane, (&acc[0][0][0])[i]);
-        }
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int tok = mt * 8 + 2 * t + h;
+                if (tok >= a.m) continue;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int col = 8 * g + 2 * q;
+                    __stcg(reinterpret_cast<float2 *>(slot + tok * kTileN + col), make_float2(v0[mt][q][h], v0[mt][q][2 + h]));
+                    if (NCOL == 2)
+                        __stcg(reinterpret_cast<float2 *>(slot + (a.m + tok) * kTileN + col), make_float2(acc[mt][q][h], acc[mt][q][2 + h]));
+                }
+            }
         __threadfence();
         __syncwarp();
         int last_one = 0;
@@ -355,18 +427,47 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(const GemvArgs a) {
         last_one = __shfl_sync(0xffffffffu, last_one, 0);
         if (!last_one) return;
         __threadfence();
-        float s0[MT][4][4], s1[MT][4][4];
-        zero(s0);
-        zero(s1);
-        for (int c = c0; c <= c1; ++c) {
-            const float *src = a.partial + static_cast<int64_t>(c + j) * (NCOL * kVals * 32);
+        // Last contributor: lane L sums the (token, column) pairs L, L + 32, ... over the contributors in
+        // chunk order (the order does not depend on timing). Two pairs and up to kC contributors are
+        // loaded at once, so the reduction costs few L2 round trips.
+        constexpr int kC = 12;
+        const int pairs = a.m * kTileN;
+        for (int p = lane; p < pairs; p += 64) {
+            const bool two = p + 32 < pairs;
+            float s0[2] = {0.0f, 0.0f}, s1[2] = {0.0f, 0.0f};
+            for (int c = c0; c <= c1; c += kC) {
+                float l0[2][kC], l1[2][kC];
 #pragma unroll
-            for (int i = 0; i < kVals; ++i) {
-                (&s0[0][0][0])[i] += __ldcg(src + i * 32 + lane);
-                if (NCOL == 2) (&s1[0][0][0])[i] += __ldcg(src + (kVals + i) * 32 + lane);
+                for (int u = 0; u < kC; ++u)
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        const bool in = c + u <= c1 && (q == 0 || two);
+                        const float *src = a.partial + static_cast<int64_t>(c + u + j) * kSlot + p + 32 * q;
+                        l0[q][u] = in ? __ldcg(src) : 0.0f;
+                        l1[q][u] = (in && NCOL == 2) ? __ldcg(src + pairs) : 0.0f;
+                    }
+#pragma unroll
+                for (int u = 0; u < kC; ++u)
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        s0[q] += l0[q][u];
+                        s1[q] += l1[q][u];
+                    }
+            }
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+                if (q == 1 && !two) break;
+                const int tok = (p + 32 * q) / kTileN, ycol = j * kTileN + (p + 32 * q) % kTileN;
+                if constexpr (EPI == HMB_EPI_SWIGLU) {
+                    static_cast<uint16_t *>(a.y)[static_cast<int64_t>(tok) * a.ldy + ycol] =
+                        static_cast<uint16_t>(to16<F16>(silu_mul_rounded<F16>(s0[q], s1[q])));
+                } else if (a.y_f32) {
+                    static_cast<float *>(a.y)[static_cast<int64_t>(tok) * a.ldy + ycol] = s0[q];
+                } else {
+                    static_cast<uint16_t *>(a.y)[static_cast<int64_t>(tok) * a.ldy + ycol] = static_cast<uint16_t>(to16<F16>(s0[q]));
+                }
             }
         }
-        epilogue<MT, F16, EPI>(a, j, g, t, s0, NCOL == 2 ? s1 : s0);
         if (lane == 0) a.counters[j] = 0;
     };
 
@@ -374,7 +475,15 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(const GemvArgs a) {
     int stage = 0;
     for (int it = b; it < e; ++it) {
         cp_async_wait<S - 2>();
-        if (it + S - 1 < e) issue();
+        if (!mbar_wait(bars + 8 * stage, ((it - b) / S) & 1)) {
+            if (lane == 0) atomicOr(a.status, 1);
+            break;
+        }
+        __syncwarp();
+        if (it + S - 1 < e) {
+            issue_w();
+            issue_x();
+        }
         cp_async_commit();
         tile_mma<MT, F16>(ring + stage * sb, wlane, xrow, g, acc);
         stage = stage + 1 == S ? 0 : stage + 1;
@@ -405,7 +514,7 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(const GemvArgs a) {
 template <int NCOL, int MT, int W, int S, int MAXM, bool F16, int EPI>
 int launch(const GemvArgs &a, cudaStream_t stream) {
     auto kernel = gemv_kernel<NCOL, MT, W, S, MAXM, F16, EPI>;
-    constexpr int smem = W * S * stage_bytes(MAXM);
+    constexpr int smem = W * S * stage_bytes(MAXM) + W * S * 8;
     static_assert(smem <= kSmemBudget, "ring too large");
     static std::mutex mu;
     static bool configured[64] = {};
@@ -422,7 +531,11 @@ int launch(const GemvArgs &a, cudaStream_t stream) {
             configured[dev] = true;
         }
     }
-    kernel<<<(a.warps + W - 1) / W, W * 32, W * S * stage_bytes(a.m), stream>>>(a);
+    const cudaError_t e = launch_pdl(kernel, dim3((a.warps + W - 1) / W), dim3(W * 32), W * S * stage_bytes(a.m) + W * S * 8, stream, a);
+    if (e != cudaSuccess) {
+        set_cuda_error(e);
+        return HMB_ERR_CUDA;
+    }
     return launch_status();
 }
 
@@ -513,6 +626,8 @@ int hmb_w4a16_gemv(const uint8_t *packed, int64_t packed_k, int64_t packed_n, co
     if (a.colsets > static_cast<int>(kCounterBytes / sizeof(int))) return HMB_ERR_UNSUPPORTED;
     const size_t need = kCounterBytes + partial_bytes(std::min<int64_t>(m, 16), a.colsets, ncol, a.warps);
     if (!workspace || workspace_bytes < need || !aligned(workspace, 16)) return HMB_ERR_WORKSPACE;
+    a.status = device_status_word();
+    if (!a.status) return HMB_ERR_CUDA;
     a.counters = static_cast<int *>(workspace);
     a.partial = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + kCounterBytes);
 
