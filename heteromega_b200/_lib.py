@@ -40,6 +40,8 @@ SIGNATURES = {
                                       _int, _vp]),
     "hmb_w4a16_gemm": (_int, [_vp, _i64, _i64, _vp, _i64, _int, _vp, _i64, _int, _i64, _i64, _i64, _i64, _int, _int, _vp]),
     "hmb_w4a16_gemm_supports": (_int, [_i64, _i64, _i64, _int]),
+    "hmb_w4a16_ffn": (_int, [_vp, _vp, _i64, _i64, _i64, _int, _vp, _i64, _int, _vp, _i64, _int, _i64, _vp, _sz, _vp]),
+    "hmb_w4a16_ffn_workspace": (_sz, [_i64, _i64, _i64]),
     "hmb_device_status": (_int, [_vp, _vp]),
     "hmb_silu_mul": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _int, _vp]),
     "hmb_residual_add2": (_int, [_vp, _i64, _vp, _i64, _int, _vp, _i64, _int, _i64, _i64, _vp]),

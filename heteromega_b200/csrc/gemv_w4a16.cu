@@ -296,105 +296,105 @@ struct Cursor {
     }
 };
 
+// One warp's share of a GEMV: its contiguous chunk of items, streamed through its private ring.
+// prefetch() requests the weight tiles of the first S - 1 items (they never depend on an earlier
+// kernel); start() requests their rows of x; run() consumes the chunk and finishes its column sets.
+// `use0` is the warp's ring use count so far (0 for a fresh ring): a kernel that ran another GEMV
+// through the same ring continues its barriers' phases from there.
 template <int NCOL, int MT, int W, int S, int MAXM, bool F16, int EPI>
-__global__ void __launch_bounds__(W * 32, 1) gemv_kernel(const GemvArgs a) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g = lane >> 2, t = lane & 3;
-    const int gw = blockIdx.x * W + warp;
-    if (gw >= a.warps) return;  // a.warps <= items: every chunk below it holds at least one tile
-    const int b = static_cast<int>(static_cast<int64_t>(gw) * a.items / a.warps);
-    const int e = static_cast<int>(static_cast<int64_t>(gw + 1) * a.items / a.warps);
-    const int per_set = NCOL * a.k_tiles;
-    const int sb = stage_bytes(a.m);
-    // Stage addresses are offsets from g_smem for loads; cp.async takes the shared-window address.
-    const uint32_t smem_base = static_cast<uint32_t>(__cvta_generic_to_shared(g_smem));
-    const uint32_t ring = warp * S * sb;
-    // This lane's 16 bytes of weight chunk c are at tile + 512 c + wlane: K rows 16c + 4t .. +3, column group g.
-    const uint32_t wlane = 256 * (t >> 1) + 32 * g + 16 * (t & 1);
-    const uint32_t bars = smem_base + W * S * sb + warp * S * 8;  // this warp's ring barriers
-    // x rows of a tile: 16 m copies of 16 bytes, taken by the lanes in turn (copy lane + 32 r).
-    const int xcopies = 16 * a.m;
+struct GemvWarp {
+    const GemvArgs &a;
+    int lane, g, t, gw, b, e, per_set, sb;
+    uint32_t smem_base, ring, wlane, bars;
     int64_t x_src[(16 * MAXM + 31) / 32];
     uint32_t x_dst[(16 * MAXM + 31) / 32];
-#pragma unroll
-    for (int r = 0; r < (16 * MAXM + 31) / 32; ++r) {
-        const int c = lane + 32 * r;
-        const int tok = c >> 4, piece = c & 15;
-        x_dst[r] = 4352 + tok * kXRowBytes + piece * 16;
-        x_src[r] = (static_cast<int64_t>(tok) * a.ldx + piece * 8) * 2;
-    }
     uint32_t xrow[MT];
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt) xrow[mt] = 4352 + min(mt * 8 + g, a.m - 1) * kXRowBytes + 8 * t;
+    Cursor in;
+    const uint8_t *in_col;
+    int use0, in_use;
 
-    auto col_tile = [&](int j, int s) {
-        const int base = (NCOL == 2 && a.col_stride == 1) ? 2 * j : j;
-        return a.col_tile0 + base + s * a.col_stride;
-    };
-    Cursor in{b / per_set, (b % per_set) / a.k_tiles, b % a.k_tiles};
-    const uint8_t *in_col = a.packed + tile_index(col_tile(in.j, in.s), 0, a.tiles_k_total, a.tiles_n_total) * kTileBytes;
-    int in_stage = 0;
-    // The weight tile of the next item, as one bulk copy (lane 0) onto the stage's barrier.
-    auto issue_w = [&]() {
+    __device__ __forceinline__ GemvWarp(const GemvArgs &args, int use_start) : a(args), use0(use_start), in_use(use_start) {
+        const int warp = threadIdx.x >> 5;
+        lane = threadIdx.x & 31;
+        g = lane >> 2;
+        t = lane & 3;
+        gw = blockIdx.x * W + warp;
+        // a.warps <= items: every chunk below it holds at least one tile; warps past it sit out.
+        b = gw < a.warps ? static_cast<int>(static_cast<int64_t>(gw) * a.items / a.warps) : 0;
+        e = gw < a.warps ? static_cast<int>(static_cast<int64_t>(gw + 1) * a.items / a.warps) : 0;
+        per_set = NCOL * a.k_tiles;
+        sb = stage_bytes(a.m);
+        smem_base = static_cast<uint32_t>(__cvta_generic_to_shared(g_smem));
+        ring = warp * S * sb;
+        // This lane's 16 bytes of weight chunk c are at tile + 512 c + wlane: K rows 16c + 4t .. +3, column group g.
+        wlane = 256 * (t >> 1) + 32 * g + 16 * (t & 1);
+        bars = smem_base + W * S * sb + warp * S * 8;
+        // x rows of a tile: 16 m copies of 16 bytes, taken by the lanes in turn (copy lane + 32 r).
+#pragma unroll
+        for (int r = 0; r < (16 * MAXM + 31) / 32; ++r) {
+            const int c = lane + 32 * r;
+            const int tok = c >> 4, piece = c & 15;
+            x_dst[r] = 4352 + tok * kXRowBytes + piece * 16;
+            x_src[r] = (static_cast<int64_t>(tok) * a.ldx + piece * 8) * 2;
+        }
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) xrow[mt] = 4352 + min(mt * 8 + g, a.m - 1) * kXRowBytes + 8 * t;
+        in = Cursor{b / per_set, (b % per_set) / a.k_tiles, b % a.k_tiles};
+        in_col = column(in);
+    }
+
+    __device__ __forceinline__ const uint8_t *column(const Cursor &c) const {
+        const int base = (NCOL == 2 && a.col_stride == 1) ? 2 * c.j : c.j;
+        return a.packed + tile_index(a.col_tile0 + base + c.s * a.col_stride, 0, a.tiles_k_total, a.tiles_n_total) * kTileBytes;
+    }
+    __device__ __forceinline__ uint32_t stage_addr(int use) const { return ring + (use % S) * sb; }
+
+    // The weight tile of the item at `in`, as one bulk copy (lane 0) onto its stage's barrier.
+    __device__ __forceinline__ void issue_w(int use) {
         if (lane == 0) {
-            const uint32_t bar = bars + 8 * in_stage;
+            const uint32_t bar = bars + 8 * (use % S);
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // after this warp's reads of the stage
             mbar_expect_tx(bar, kTileBytes);
-            bulk_load(smem_base + ring + in_stage * sb, in_col + static_cast<int64_t>(in.kt) * kTileBytes, kTileBytes, bar);
+            bulk_load(smem_base + stage_addr(use), in_col + static_cast<int64_t>(in.kt) * kTileBytes, kTileBytes, bar);
         }
-    };
-    // Its rows of x (cp.async, one commit group per tile), then advance to the next item.
-    auto issue_x = [&]() {
+    }
+    // Rows of x of the item at `in` (cp.async, one commit group per tile), then advance `in`.
+    __device__ __forceinline__ void issue_x(int use) {
         const uint8_t *xsrc = reinterpret_cast<const uint8_t *>(a.x + in.kt * kTileK);
-        const uint32_t dst = smem_base + ring + in_stage * sb;
+        const uint32_t dst = smem_base + stage_addr(use);
 #pragma unroll
         for (int r = 0; r < (16 * MAXM + 31) / 32; ++r)
-            if (lane + 32 * r < xcopies) cp_async16(dst + x_dst[r], xsrc + x_src[r]);
+            if (lane + 32 * r < 16 * a.m) cp_async16(dst + x_dst[r], xsrc + x_src[r]);
+        advance();
+    }
+    __device__ __forceinline__ void advance() {
         const int j0 = in.j, s0 = in.s;
         in.next(a.k_tiles, NCOL);
-        if (in.j != j0 || in.s != s0) {
-            in_col = a.packed + tile_index(col_tile(in.j, in.s), 0, a.tiles_k_total, a.tiles_n_total) * kTileBytes;
-        }
-        if (++in_stage == S) in_stage = 0;
-    };
-
-    pdl_launch_dependents();
-    if (lane == 0) {
-        for (int q = 0; q < S; ++q) mbar_init(bars + 8 * q, 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        if (in.j != j0 || in.s != s0) in_col = column(in);
     }
-    __syncwarp();
-    // Weights of the first S - 1 items before the previous kernel has finished; everything that
-    // kernel may write (x) or read (y, the workspace) only after pdl_wait().
-    {
+
+    __device__ __forceinline__ void prefetch() {
         const Cursor in0 = in;
         const uint8_t *in_col0 = in_col;
-        for (int p = 0; p < S - 1; ++p) {
-            if (b + p < e) {
-                issue_w();
-                in.next(a.k_tiles, NCOL);
-                if (++in_stage == S) in_stage = 0;
-                in_col = a.packed + tile_index(col_tile(in.j, in.s), 0, a.tiles_k_total, a.tiles_n_total) * kTileBytes;
-            }
+        for (int p = 0; p < S - 1 && b + p < e; ++p) {
+            issue_w(use0 + p);
+            advance();
         }
         in = in0;
         in_col = in_col0;
-        in_stage = 0;
     }
-    pdl_wait();
+    __device__ __forceinline__ void start() {
 #pragma unroll
-    for (int p = 0; p < S - 1; ++p) {
-        if (b + p < e) issue_x();
-        cp_async_commit();
+        for (int p = 0; p < S - 1; ++p) {
+            if (b + p < e) issue_x(use0 + p);
+            cp_async_commit();
+        }
+        in_use = use0 + S - 1;
     }
 
-    float acc[MT][4][4], gate[MT][4][4];
-    zero(acc);
-    zero(gate);
-
-    // Finish column set j from acc (slot NCOL-1) and gate (slot 0 when NCOL == 2): from registers if
-    // this chunk holds all of it, else as a contributor.
-    auto finish = [&](int j) {
+    // Finishes column set j from acc (slot NCOL-1) and gate (slot 0 when NCOL == 2): from registers
+    // if this chunk holds all of it, else as a contributor.
+    __device__ __forceinline__ void finish(int j, const float (&gate)[MT][4][4], const float (&acc)[MT][4][4]) {
         const float(&v0)[MT][4][4] = NCOL == 2 ? gate : acc;
         const int first = j * per_set, last = first + per_set - 1;
         if (first >= b && last < e) {
@@ -441,10 +441,10 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(const GemvArgs a) {
                 for (int u = 0; u < kC; ++u)
 #pragma unroll
                     for (int q = 0; q < 2; ++q) {
-                        const bool in = c + u <= c1 && (q == 0 || two);
+                        const bool ok = c + u <= c1 && (q == 0 || two);
                         const float *src = a.partial + static_cast<int64_t>(c + u + j) * kSlot + p + 32 * q;
-                        l0[q][u] = in ? __ldcg(src) : 0.0f;
-                        l1[q][u] = (in && NCOL == 2) ? __ldcg(src + pairs) : 0.0f;
+                        l0[q][u] = ok ? __ldcg(src) : 0.0f;
+                        l1[q][u] = (ok && NCOL == 2) ? __ldcg(src + pairs) : 0.0f;
                     }
 #pragma unroll
                 for (int u = 0; u < kC; ++u)
@@ -469,46 +469,79 @@ __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(const GemvArgs a) {
             }
         }
         if (lane == 0) a.counters[j] = 0;
-    };
-
-    Cursor cur{b / per_set, (b % per_set) / a.k_tiles, b % a.k_tiles};
-    int stage = 0;
-    for (int it = b; it < e; ++it) {
-        cp_async_wait<S - 2>();
-        if (!mbar_wait(bars + 8 * stage, ((it - b) / S) & 1)) {
-            if (lane == 0) atomicOr(a.status, 1);
-            break;
-        }
-        __syncwarp();
-        if (it + S - 1 < e) {
-            issue_w();
-            issue_x();
-        }
-        cp_async_commit();
-        tile_mma<MT, F16>(ring + stage * sb, wlane, xrow, g, acc);
-        stage = stage + 1 == S ? 0 : stage + 1;
-        const int j0 = cur.j, s0 = cur.s;
-        cur.next(a.k_tiles, NCOL);
-        const bool set_done = cur.j != j0 || it + 1 == e;
-        // acc holds the slot in progress; gate sums move aside when the up tiles start or the chunk ends on them.
-        if (NCOL == 2 && s0 == 0 && (set_done || cur.s == 1)) {
-#pragma unroll
-            for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-                for (int q = 0; q < 4; ++q)
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        gate[mt][q][i] = acc[mt][q][i];
-                        acc[mt][q][i] = 0.0f;
-                    }
-        }
-        if (set_done) {
-            finish(j0);
-            zero(acc);
-            zero(gate);
-        }
     }
-    cp_async_wait<0>();
+
+    // Consumes the chunk; returns the warp's ring use count afterwards.
+    __device__ __forceinline__ int run() {
+        float acc[MT][4][4], gate[MT][4][4];
+        zero(acc);
+        zero(gate);
+        Cursor cur{b / per_set, (b % per_set) / a.k_tiles, b % a.k_tiles};
+        int use = use0;
+        for (int it = b; it < e; ++it, ++use) {
+            cp_async_wait<S - 2>();
+            if (!mbar_wait(bars + 8 * (use % S), (use / S) & 1)) {
+                if (lane == 0) atomicOr(a.status, 1);
+                break;
+            }
+            __syncwarp();
+            if (it + S - 1 < e) {
+                issue_w(in_use);
+                issue_x(in_use);
+                ++in_use;
+            }
+            cp_async_commit();
+            tile_mma<MT, F16>(stage_addr(use), wlane, xrow, g, acc);
+            const int j0 = cur.j, s0 = cur.s;
+            cur.next(a.k_tiles, NCOL);
+            const bool set_done = cur.j != j0 || it + 1 == e;
+            // acc holds the slot in progress; gate sums move aside when the up tiles start or the chunk ends on them.
+            if (NCOL == 2 && s0 == 0 && (set_done || cur.s == 1)) {
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            gate[mt][q][i] = acc[mt][q][i];
+                            acc[mt][q][i] = 0.0f;
+                        }
+            }
+            if (set_done) {
+                finish(j0, gate, acc);
+                zero(acc);
+                zero(gate);
+            }
+        }
+        cp_async_wait<0>();
+        return use0 + (e - b);
+    }
+};
+
+// Initialises this warp's S ring barriers (one expected arrival each: the bulk copy's arrive.expect_tx).
+template <int W, int S>
+__device__ __forceinline__ void init_ring_barriers(int sb) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        const uint32_t bars = static_cast<uint32_t>(__cvta_generic_to_shared(g_smem)) + W * S * sb + warp * S * 8;
+        for (int q = 0; q < S; ++q) mbar_init(bars + 8 * q, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+}
+
+template <int NCOL, int MT, int W, int S, int MAXM, bool F16, int EPI>
+__global__ void __launch_bounds__(W * 32, 1) gemv_kernel(const GemvArgs a) {
+    if (static_cast<int>(blockIdx.x * W + (threadIdx.x >> 5)) >= a.warps) return;
+    pdl_launch_dependents();
+    init_ring_barriers<W, S>(stage_bytes(a.m));
+    GemvWarp<NCOL, MT, W, S, MAXM, F16, EPI> w(a, 0);
+    // Weights of the first S - 1 items before the previous kernel has finished; everything that
+    // kernel may write (x) or read (y, the workspace) only after pdl_wait().
+    w.prefetch();
+    pdl_wait();
+    w.start();
+    w.run();
 }
 
 template <int NCOL, int MT, int W, int S, int MAXM, bool F16, int EPI>
@@ -572,6 +605,59 @@ size_t partial_bytes(int64_t m, int64_t colsets, int ncol, int64_t warps) {
     return static_cast<size_t>(warps + colsets) * ncol * mt * 16 * 32 * sizeof(float);
 }
 
+// Validates a GEMV over [k x n] of a [packed_k x packed_n] matrix and fills every field of `a` but x,
+// y, m, counters and partial; `partial` receives the bytes of contributor slots it needs. For the
+// SwiGLU blocked layout the up columns start up_tiles tile columns after the gate ones (0: n / 2).
+int gemv_args(GemvArgs &a, size_t &partial, const uint8_t *packed, int64_t packed_k, int64_t packed_n, int64_t ldx, int x_dtype,
+              int64_t ldy, int y_dtype, int64_t m, int64_t k, int64_t n, int64_t start_col, int epilogue, int layout, int split_k,
+              int64_t up_tiles) {
+    if (!packed || m <= 0) return HMB_ERR_ARG;
+    if (k <= 0 || n <= 0 || k % kTileK || n % kTileN || packed_k % kTileK || packed_n % kTileN || start_col < 0 ||
+        start_col % kTileN || k > packed_k || start_col + n > packed_n)
+        return HMB_ERR_ARG;
+    if (x_dtype != HMB_BF16 && x_dtype != HMB_FP16) return HMB_ERR_ARG;
+    if (epilogue != HMB_EPI_STORE && epilogue != HMB_EPI_SWIGLU) return HMB_ERR_ARG;
+    if (y_dtype != x_dtype && !(y_dtype == HMB_FP32 && epilogue == HMB_EPI_STORE)) return HMB_ERR_ARG;
+    if (epilogue == HMB_EPI_SWIGLU) {
+        if (layout != HMB_GATE_UP_BLOCKED && layout != HMB_GATE_UP_INTERLEAVED) return HMB_ERR_ARG;
+        if (n % (2 * kTileN)) return HMB_ERR_ARG;
+    }
+    const int64_t out_cols = epilogue == HMB_EPI_SWIGLU ? n / 2 : n;
+    if (ldx < k || ldy < out_cols || ldx % 8 || ldy % 8) return ldx < k || ldy < out_cols ? HMB_ERR_ARG : HMB_ERR_ALIGN;
+    if (!aligned(packed, 16)) return HMB_ERR_ALIGN;
+    if (packed_k / kTileK > (1 << 30) || packed_n / kTileN > (1 << 30)) return HMB_ERR_UNSUPPORTED;
+    a = GemvArgs{};
+    a.packed = packed;
+    a.tiles_k_total = static_cast<int>(packed_k / kTileK);
+    a.tiles_n_total = static_cast<int>(packed_n / kTileN);
+    a.col_tile0 = static_cast<int>(start_col / kTileN);
+    a.k_tiles = static_cast<int>(k / kTileK);
+    const int n_tiles = static_cast<int>(n / kTileN);
+    a.ldx = ldx;
+    a.ldy = ldy;
+    a.y_f32 = y_dtype == HMB_FP32;
+    const int ncol = epilogue == HMB_EPI_SWIGLU ? 2 : 1;
+    a.colsets = n_tiles / ncol;
+    a.col_stride = epilogue == HMB_EPI_SWIGLU
+                       ? (layout == HMB_GATE_UP_INTERLEAVED ? 1 : static_cast<int>(up_tiles > 0 ? up_tiles : n_tiles / 2))
+                       : 0;
+    if (epilogue == HMB_EPI_SWIGLU && layout == HMB_GATE_UP_BLOCKED && a.col_tile0 + a.col_stride + a.colsets > a.tiles_n_total)
+        return HMB_ERR_ARG;
+    const int64_t items = static_cast<int64_t>(a.colsets) * ncol * a.k_tiles;
+    if (items > (1LL << 30)) return HMB_ERR_UNSUPPORTED;
+    a.items = static_cast<int>(items);
+    a.warps = static_cast<int>(grid_warps(items, split_k, std::min<int64_t>(m, 16)));
+    if (a.colsets > static_cast<int>(kCounterBytes / sizeof(int))) return HMB_ERR_UNSUPPORTED;
+    partial = partial_bytes(std::min<int64_t>(m, 16), a.colsets, ncol, a.warps);
+    a.status = device_status_word();
+    if (!a.status) return HMB_ERR_CUDA;
+    return HMB_OK;
+}
+
+// Workspace of hmb_w4a16_ffn: [gate/up counters][down counters][act][gate/up slots][down slots]. The
+// prefill (GEMM) path uses act only; the counters stay zero for the decode path.
+size_t round256(size_t b) { return (b + 255) / 256 * 256; }
+
 }  // namespace
 }  // namespace hmb
 
@@ -590,44 +676,13 @@ size_t hmb_w4a16_gemv_workspace(int64_t m, int64_t k, int64_t n, int epilogue, i
 int hmb_w4a16_gemv(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const void *x, int64_t ldx, int x_dtype, void *y,
                    int64_t ldy, int y_dtype, int64_t m, int64_t k, int64_t n, int64_t start_col, int epilogue, int layout,
                    int split_k, void *workspace, size_t workspace_bytes, hmb_stream_t stream) {
-    if (!packed || !x || !y || m <= 0) return HMB_ERR_ARG;
-    if (k <= 0 || n <= 0 || k % kTileK || n % kTileN || packed_k % kTileK || packed_n % kTileN || start_col < 0 ||
-        start_col % kTileN || k > packed_k || start_col + n > packed_n)
-        return HMB_ERR_ARG;
-    if (x_dtype != HMB_BF16 && x_dtype != HMB_FP16) return HMB_ERR_ARG;
-    if (epilogue != HMB_EPI_STORE && epilogue != HMB_EPI_SWIGLU) return HMB_ERR_ARG;
-    if (y_dtype != x_dtype && !(y_dtype == HMB_FP32 && epilogue == HMB_EPI_STORE)) return HMB_ERR_ARG;
-    if (epilogue == HMB_EPI_SWIGLU) {
-        if (layout != HMB_GATE_UP_BLOCKED && layout != HMB_GATE_UP_INTERLEAVED) return HMB_ERR_ARG;
-        if (n % (2 * kTileN)) return HMB_ERR_ARG;
-    }
-    const int64_t out_cols = epilogue == HMB_EPI_SWIGLU ? n / 2 : n;
-    if (ldx < k || ldy < out_cols) return HMB_ERR_ARG;
-    if (!aligned(packed, 16) || !aligned(x, 16) || !aligned(y, 16) || ldx % 8 || ldy % 8) return HMB_ERR_ALIGN;
-    if (packed_k / kTileK > (1 << 30) || packed_n / kTileN > (1 << 30)) return HMB_ERR_UNSUPPORTED;
-
-    GemvArgs a{};
-    a.packed = packed;
-    a.tiles_k_total = static_cast<int>(packed_k / kTileK);
-    a.tiles_n_total = static_cast<int>(packed_n / kTileN);
-    a.col_tile0 = static_cast<int>(start_col / kTileN);
-    a.k_tiles = static_cast<int>(k / kTileK);
-    const int n_tiles = static_cast<int>(n / kTileN);
-    a.ldx = ldx;
-    a.ldy = ldy;
-    a.y_f32 = y_dtype == HMB_FP32;
-    const int ncol = epilogue == HMB_EPI_SWIGLU ? 2 : 1;
-    a.colsets = n_tiles / ncol;
-    a.col_stride = epilogue == HMB_EPI_SWIGLU ? (layout == HMB_GATE_UP_INTERLEAVED ? 1 : n_tiles / 2) : 0;
-    const int64_t items = static_cast<int64_t>(a.colsets) * ncol * a.k_tiles;
-    if (items > (1LL << 30)) return HMB_ERR_UNSUPPORTED;
-    a.items = static_cast<int>(items);
-    a.warps = static_cast<int>(grid_warps(items, split_k, std::min<int64_t>(m, 16)));
-    if (a.colsets > static_cast<int>(kCounterBytes / sizeof(int))) return HMB_ERR_UNSUPPORTED;
-    const size_t need = kCounterBytes + partial_bytes(std::min<int64_t>(m, 16), a.colsets, ncol, a.warps);
-    if (!workspace || workspace_bytes < need || !aligned(workspace, 16)) return HMB_ERR_WORKSPACE;
-    a.status = device_status_word();
-    if (!a.status) return HMB_ERR_CUDA;
+    if (!x || !y) return HMB_ERR_ARG;
+    GemvArgs a;
+    size_t partial = 0;
+    int rc = gemv_args(a, partial, packed, packed_k, packed_n, ldx, x_dtype, ldy, y_dtype, m, k, n, start_col, epilogue, layout, split_k, 0);
+    if (rc != HMB_OK) return rc;
+    if (!aligned(x, 16) || !aligned(y, 16)) return HMB_ERR_ALIGN;
+    if (!workspace || workspace_bytes < kCounterBytes + partial || !aligned(workspace, 16)) return HMB_ERR_WORKSPACE;
     a.counters = static_cast<int *>(workspace);
     a.partial = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) + kCounterBytes);
 
@@ -636,7 +691,70 @@ int hmb_w4a16_gemv(const uint8_t *packed, int64_t packed_k, int64_t packed_n, co
         a.m = static_cast<int>(std::min<int64_t>(16, m - r0));
         a.x = static_cast<const uint16_t *>(x) + r0 * ldx;
         a.y = static_cast<uint8_t *>(y) + r0 * ldy * y_elem;
-        const int rc = x_dtype == HMB_FP16 ? dispatch<true>(a, epilogue, stream) : dispatch<false>(a, epilogue, stream);
+        rc = x_dtype == HMB_FP16 ? dispatch<true>(a, epilogue, stream) : dispatch<false>(a, epilogue, stream);
+        if (rc != HMB_OK) return rc;
+    }
+    return HMB_OK;
+}
+
+size_t hmb_w4a16_ffn_workspace(int64_t m, int64_t h, int64_t n) {
+    if (m <= 0 || h <= 0 || n <= 0 || h % kTileK || n % kTileK) return 0;
+    const int64_t rows = std::min<int64_t>(m, 16);
+    const int64_t gu_items = (2 * n / kTileN) * (h / kTileK), dn_items = (h / kTileN) * (n / kTileK);
+    return 2 * kCounterBytes + round256(static_cast<size_t>(m) * n * 2) +
+           round256(partial_bytes(rows, n / kTileN, 2, grid_warps(gu_items, 0, rows))) +
+           round256(partial_bytes(rows, h / kTileN, 1, grid_warps(dn_items, 0, rows)));
+}
+
+int hmb_w4a16_ffn(const uint8_t *gate_up, const uint8_t *down, int64_t h, int64_t n, int64_t stored, int layout, const void *x,
+                  int64_t ldx, int x_dtype, void *y, int64_t ldy, int y_dtype, int64_t m, void *workspace, size_t workspace_bytes,
+                  hmb_stream_t stream) {
+    if (!gate_up || !down || !x || !y || m <= 0 || h <= 0 || n <= 0 || stored <= 0) return HMB_ERR_ARG;
+    if (h % kTileK || n % kTileK || stored % kTileK || n > stored) return HMB_ERR_ARG;
+    if (layout != HMB_GATE_UP_BLOCKED && layout != HMB_GATE_UP_INTERLEAVED) return HMB_ERR_ARG;
+    if (!aligned(x, 16) || !aligned(y, 16) || !workspace || !aligned(workspace, 256)) return workspace ? HMB_ERR_ALIGN : HMB_ERR_WORKSPACE;
+    if (workspace_bytes < hmb_w4a16_ffn_workspace(m, h, n)) return HMB_ERR_WORKSPACE;
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    const size_t act_off = 2 * kCounterBytes;
+
+    // Prefill: the tcgen05 GEMMs, gate/up with the SwiGLU epilogue into act, then down.
+    const bool same_up = layout == HMB_GATE_UP_INTERLEAVED || n == stored;
+    if (m > 16 && same_up && hmb_w4a16_gemm_supports(m, h, 2 * n, HMB_EPI_SWIGLU) && hmb_w4a16_gemm_supports(m, n, h, HMB_EPI_STORE)) {
+        void *act = ws + act_off;
+        int rc = hmb_w4a16_gemm(gate_up, h, 2 * stored, x, ldx, x_dtype, act, n, x_dtype, m, h, 2 * n, 0, HMB_EPI_SWIGLU, layout, stream);
+        if (rc != HMB_OK) return rc;
+        return hmb_w4a16_gemm(down, stored, h, act, n, x_dtype, y, ldy, y_dtype, m, n, h, 0, HMB_EPI_STORE, 0, stream);
+    }
+
+    // Decode: the gate/up GEMV with the SwiGLU epilogue into act, then the down GEMV, per 16 rows. The
+    // down GEMV is a programmatic dependent of the first: it requests its weights while gate/up ends.
+    GemvArgs gu, dn;
+    size_t gu_partial = 0, dn_partial = 0;
+    int rc = gemv_args(gu, gu_partial, gate_up, h, 2 * stored, ldx, x_dtype, n, x_dtype, m, h, 2 * n, 0, HMB_EPI_SWIGLU, layout, 0,
+                       stored / kTileN);
+    if (rc != HMB_OK) return rc;
+    rc = gemv_args(dn, dn_partial, down, stored, h, n, x_dtype, ldy, y_dtype, m, n, h, 0, HMB_EPI_STORE, 0, 0, 0);
+    if (rc != HMB_OK) return rc;
+    size_t off = 0;
+    gu.counters = reinterpret_cast<int *>(ws + off);
+    off += kCounterBytes;
+    dn.counters = reinterpret_cast<int *>(ws + off);
+    off += kCounterBytes;
+    uint16_t *act = reinterpret_cast<uint16_t *>(ws + off);
+    off += round256(static_cast<size_t>(m) * n * 2);
+    gu.partial = reinterpret_cast<float *>(ws + off);
+    off += round256(gu_partial);
+    dn.partial = reinterpret_cast<float *>(ws + off);
+    const size_t y_elem = y_dtype == HMB_FP32 ? 4 : 2;
+    for (int64_t r0 = 0; r0 < m; r0 += 16) {
+        gu.m = dn.m = static_cast<int>(std::min<int64_t>(16, m - r0));
+        gu.x = static_cast<const uint16_t *>(x) + r0 * ldx;
+        gu.y = act;
+        dn.x = act;
+        dn.y = static_cast<uint8_t *>(y) + r0 * ldy * y_elem;
+        rc = x_dtype == HMB_FP16 ? dispatch<true>(gu, HMB_EPI_SWIGLU, stream) : dispatch<false>(gu, HMB_EPI_SWIGLU, stream);
+        if (rc != HMB_OK) return rc;
+        rc = x_dtype == HMB_FP16 ? dispatch<true>(dn, HMB_EPI_STORE, stream) : dispatch<false>(dn, HMB_EPI_STORE, stream);
         if (rc != HMB_OK) return rc;
     }
     return HMB_OK;

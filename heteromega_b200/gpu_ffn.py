@@ -319,16 +319,10 @@ class GpuFfnBuffers:
         return GpuFfnBuffers(torch.empty(0, **opt), torch.empty(max_m * channels, **opt), torch.empty(0, **opt))
 
 
-def _act_buffer(buf, m, n, device):
-    if buf is not None and buf.act is not None and buf.act.numel() >= m * n:
-        return buf.act.view(-1)[:m * n].view(m, n)
-    return torch.empty(m, n, dtype=torch.bfloat16, device=device)
-
-
 def gpu_ffn_slice_forward(w, x_norm, buf, y, stream=None):
-    """GPU share of one FFN sublayer (gpu_ffn.hpp:173-183): enqueues the fused gate/up + SiLU*up
-    kernel and the down kernel on `stream`; does not synchronize.
-    x_norm and y: bf16 [M, H], contiguous rows."""
+    """GPU share of one FFN sublayer (gpu_ffn.hpp:173-183): enqueues the gate/up + SiLU*up and down
+    work on `stream` (hmb_w4a16_ffn); does not synchronize. x_norm and y: bf16 [M, H], contiguous rows
+    (y may be fp32 for unrounded partial sums)."""
     n, stored, h = w.channels(), w.stored_channels(), w.hidden
     if n != stored and w.layout != GateUpLayout.kInterleaved:
         raise ValueError("gpu_ffn_slice_forward: a prefix of the packed channels needs GateUpLayout::kInterleaved")
@@ -338,9 +332,9 @@ def gpu_ffn_slice_forward(w, x_norm, buf, y, stream=None):
     if tuple(y.shape) != (m, h):
         raise ValueError("gpu_ffn_slice_forward: y must be [M, H]")
     with _stream_ctx(stream):
-        act = _act_buffer(buf, m, n, x_norm.device)
-        w4a16_linear(act, x_norm, w.gate_up, h, 2 * n, h, 2 * stored, 0, _lib.HMB_EPI_SWIGLU, int(w.layout))
-        w4a16_linear(y, act, w.down, n, h, stored, h, 0, _lib.HMB_EPI_STORE)
+        # One call: a single fused launch for decode (m <= 16), the two tcgen05 GEMMs for prefill; the
+        # intermediate act lives in the library's workspace, so `buf` is not needed.
+        ops.w4a16_ffn(y, x_norm, w.gate_up, w.down, h, n, stored, int(w.layout))
 
 
 def packed_linear(out, inp, packed, k, n, stream=None, opt=None):

@@ -12,10 +12,9 @@ to bf16 once, as residual_add2 does.
 import torch
 import torch.distributed as dist
 
-from . import _lib
 from .gpu_ffn import FfnSliceWeights, GateUpLayout, slice_packed_ffn
 from .partition import plan_shards
-from .torch_ops import w4a16_linear
+from .torch_ops import ops
 
 
 class TensorParallelFfn:
@@ -53,11 +52,7 @@ class TensorParallelFfn:
         """partial[m, H] (fp32) = this rank's share of FFN layer `layer` for x [m, H] (bf16)."""
         w = self.layers[layer]
         n, stored, h = w.channels(), w.stored_channels(), w.hidden
-        m = x.shape[0]
-        if act is None:
-            act = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
-        w4a16_linear(act, x, w.gate_up, h, 2 * n, h, 2 * stored, 0, _lib.HMB_EPI_SWIGLU, int(w.layout))
-        w4a16_linear(partial, act, w.down, n, h, stored, h, 0, _lib.HMB_EPI_STORE)
+        ops.w4a16_ffn(partial, x, w.gate_up, w.down, h, n, stored, int(w.layout))
         return partial
 
     def reduce_partials(self, partial):

@@ -24,11 +24,12 @@ def _ptr(t):
     return t.data_ptr() if t is not None else None
 
 
-def workspace(device, nbytes):
-    """A zero-filled uint8 buffer of at least nbytes for the current stream of `device`.
-    Calls on one stream reuse it; the kernels leave its counter words zero."""
+def workspace(device, nbytes, kind="gemv"):
+    """A zero-filled uint8 buffer of at least nbytes for the current stream of `device`, one per kind
+    of call (their layouts differ). Calls on one stream reuse it; the kernels leave its counter words
+    zero."""
     stream = torch.cuda.current_stream(device)
-    key = (device.index, stream.cuda_stream)
+    key = (device.index, stream.cuda_stream, kind)
     with _ws_lock:
         buf = _workspaces.get(key)
         if buf is None or buf.numel() < nbytes:
@@ -70,6 +71,7 @@ _defs.define("w4a16_gemv(Tensor(a!) out, Tensor x, Tensor packed, int k, int n, 
              "int start_col, int epilogue, int layout, int split_k) -> ()")
 _defs.define("w4a16_gemm(Tensor(a!) out, Tensor x, Tensor packed, int k, int n, int packed_k, int packed_n, "
              "int start_col, int epilogue, int layout) -> ()")
+_defs.define("w4a16_ffn(Tensor(a!) y, Tensor x, Tensor gate_up, Tensor down, int h, int n, int stored, int layout) -> ()")
 _defs.define("w4a16_dequant(Tensor(a!) out, Tensor packed, int k, int n, int packed_k, int packed_n) -> ()")
 _defs.define("silu_mul(Tensor gate_up, Tensor(a!) act, int layout) -> ()")
 _defs.define("residual_add2(Tensor(a!) x, Tensor y_g, Tensor y_n) -> ()")
@@ -111,6 +113,27 @@ def _w4a16_gemm(out, x, packed, k, n, packed_k, packed_n, start_col, epilogue, l
     check(lib().hmb_w4a16_gemm(packed.data_ptr(), packed_k, packed_n, x.data_ptr(), x.stride(0), _dtype_code(x),
                                out.data_ptr(), out.stride(0), _dtype_code(out), m, k, n, start_col, epilogue, layout,
                                _stream(x)), "w4a16_gemm")
+
+
+def _w4a16_ffn(y, x, gate_up, down, h, n, stored, layout):
+    _check_cuda(y, x, gate_up, down)
+    if x.dim() != 2 or y.dim() != 2 or x.stride(1) != 1 or y.stride(1) != 1 or x.shape[1] != h or y.shape[1] != h:
+        raise ValueError(f"w4a16_ffn: x and y must be [M, {h}] with contiguous rows")
+    m = x.shape[0]
+    if y.shape[0] != m:
+        raise ValueError("w4a16_ffn: x and y must have the same number of rows")
+    if y.dtype != x.dtype and y.dtype != torch.float32:
+        raise ValueError("w4a16_ffn: y must have the activation dtype, or fp32 for partial sums")
+    for name, p, pk, pn in (("gate_up", gate_up, h, 2 * stored), ("down", down, stored, h)):
+        if p.dtype != torch.uint8 or not p.is_contiguous():
+            raise ValueError(f"w4a16_ffn: {name} must be contiguous uint8")
+        if p.numel() != lib().hmb_packed_bytes(pk, pn):
+            raise ValueError(f"w4a16_ffn: {name} has {p.numel()} bytes, not those of [{pk}, {pn}]")
+    ws_bytes = lib().hmb_w4a16_ffn_workspace(m, h, n)
+    ws = workspace(x.device, ws_bytes, "ffn")
+    check(lib().hmb_w4a16_ffn(gate_up.data_ptr(), down.data_ptr(), h, n, stored, layout, x.data_ptr(), x.stride(0),
+                              _dtype_code(x), y.data_ptr(), y.stride(0), _dtype_code(y), m, ws.data_ptr(), ws.numel(),
+                              _stream(x)), "w4a16_ffn")
 
 
 def gemm_supported(m, k, n, epilogue):
@@ -199,6 +222,7 @@ def _pack_w4a16_device(out, q, scales, zeros, bad):
 _impls = torch.library.Library("heteromega", "IMPL", "CUDA")
 _impls.impl("w4a16_gemv", _w4a16_gemv)
 _impls.impl("w4a16_gemm", _w4a16_gemm)
+_impls.impl("w4a16_ffn", _w4a16_ffn)
 _impls.impl("w4a16_dequant", _w4a16_dequant)
 _impls.impl("silu_mul", _silu_mul)
 _impls.impl("residual_add2", _residual_add2)

@@ -150,6 +150,22 @@ int hmb_w4a16_gemm(const uint8_t *packed, int64_t packed_k, int64_t packed_n, co
                    hmb_stream_t stream);
 int hmb_w4a16_gemm_supports(int64_t m, int64_t k, int64_t n, int epilogue);
 
+/* One SwiGLU FFN (or the FFN slice of one rank) end to end: y[m, h] = (SiLU(x Wg) * (x Wu)) Wd over
+ * channels [0, n). gate_up is the packed [h x 2 stored] matrix in `layout` order (HMB_GATE_UP_BLOCKED
+ * with n < stored: up columns start at tile column stored / 64), down the packed [stored x h] matrix
+ * whose first n rows are used. y_dtype: x_dtype, or HMB_FP32 for the unrounded partial sums that a
+ * tensor-parallel rank reduces. m <= 16 (decode) runs the gate/up GEMV with the SwiGLU epilogue and the
+ * down GEMV per 16 rows, the second launched as a programmatic dependent of the first (it requests its
+ * weights while gate/up finishes). Larger m runs the two tcgen05 GEMMs. act lives in the workspace
+ * (hmb_w4a16_ffn_workspace bytes, 256-byte aligned, zero-filled once before the first call and then
+ * left to the library: it resets what it uses). h, n and stored are multiples of 128.
+ * Replaces heteromega::gemm_w4a16_ffn (kernels/gpu/include/heteromega/gpu_ffn.hpp:113-114,
+ * kernels/gpu/src/gemm_w4a16.cu:463-502) and the GPU part of gpu_ffn_slice_forward (gpu_ffn.hpp:182-183). */
+int hmb_w4a16_ffn(const uint8_t *gate_up, const uint8_t *down, int64_t h, int64_t n, int64_t stored, int layout, const void *x,
+                  int64_t ldx, int x_dtype, void *y, int64_t ldy, int y_dtype, int64_t m, void *workspace, size_t workspace_bytes,
+                  hmb_stream_t stream);
+size_t hmb_w4a16_ffn_workspace(int64_t m, int64_t h, int64_t n);
+
 /* Reads and clears the device status word of the current device: *status = HMB_ERR_TIMEOUT if a kernel
  * gave up a bounded wait since the last call, else HMB_OK. Synchronizes `stream`. */
 int hmb_device_status(int *status, hmb_stream_t stream);
