@@ -10,6 +10,8 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(PKG, "libhmb.so")
 
 HMB_OK = 0
+# hmb_status (include/hmb.h)
+HMB_ERR_ARG, HMB_ERR_ALIGN, HMB_ERR_VALUE, HMB_ERR_WORKSPACE, HMB_ERR_UNSUPPORTED, HMB_ERR_CUDA, HMB_ERR_TIMEOUT = -1, -2, -3, -4, -5, -6, -7
 HMB_BF16, HMB_FP16, HMB_FP32 = 0, 1, 2
 HMB_GATE_UP_BLOCKED, HMB_GATE_UP_INTERLEAVED = 0, 1
 HMB_EPI_STORE, HMB_EPI_SWIGLU = 0, 1
@@ -42,6 +44,7 @@ SIGNATURES = {
     "hmb_w4a16_gemm_supports": (_int, [_i64, _i64, _i64, _int]),
     "hmb_w4a16_ffn": (_int, [_vp, _vp, _i64, _i64, _i64, _int, _vp, _i64, _int, _vp, _i64, _int, _i64, _vp, _sz, _vp]),
     "hmb_w4a16_ffn_workspace": (_sz, [_i64, _i64, _i64]),
+    "hmb_selftest_bounded_wait": (_int, [_i64, _vp]),
     "hmb_device_status": (_int, [_vp, _vp]),
     "hmb_silu_mul": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _int, _vp]),
     "hmb_residual_add2": (_int, [_vp, _i64, _vp, _i64, _int, _vp, _i64, _int, _i64, _i64, _vp]),

@@ -133,10 +133,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     cluster_sync();  // the peer's barriers are initialised before anyone arrives on them
     fence_after_sync();
     const uint32_t tmem = *tmem_slot;
+    // Programmatic dependent launch: the packed weights (constant) stream in at once; x, which the
+    // previous kernel may write, and y, which it may read, wait for it to complete.
+    pdl_launch_dependents();
 
     if (warp == kWarpX) {
         if (lane == 0) {
             prefetch_tensormap(&tmap_x);
+            pdl_wait();
             int it = 0;
             bool ok = true;
             for (int tile = cluster; ok && tile < a.num_tiles; tile += nclusters) {
@@ -274,6 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // Epilogue: warp q = warp % 4 reads TMEM lanes 32 q .. 32 q + 31 (rows of this CTA).
         const int q = warp & 3;
+        pdl_wait();
         int t = 0;
         for (int tile = cluster; tile < a.num_tiles; tile += nclusters, ++t) {
             const int acc = t % kAccStages;
@@ -364,16 +369,18 @@ int launch(const CUtensorMap &map, const PairArgs &a, cudaStream_t stream) {
     cudaGetDevice(&dev);
     if (dev >= 64) return HMB_ERR_UNSUPPORTED;
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = kSmemBytes;
     cfg.stream = stream;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 1;  // the occupancy query takes the cluster shape only
     {
         std::lock_guard<std::mutex> lock(mu);
         if (max_clusters[dev] == 0) {
@@ -392,6 +399,7 @@ int launch(const CUtensorMap &map, const PairArgs &a, cudaStream_t stream) {
     }
     const int clusters = std::min(a.num_tiles, max_clusters[dev]);
     cfg.gridDim = dim3(2 * clusters);
+    cfg.numAttrs = 2;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, map, a);
     if (e != cudaSuccess) {
         set_cuda_error(e);

@@ -119,11 +119,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     __syncthreads();
     fence_after_sync();
     const uint32_t tmem = *tmem_slot;
+    pdl_launch_dependents();
 
     if (warp == 0) {
         if (lane == 0) {
-            // Producer.
+            // Producer. x (and the y the epilogue writes) wait for the previous kernel to complete.
             prefetch_tensormap(&tmap_x);
+            pdl_wait();
             const uint8_t *col_base[4];
             for (int d = 0; d < 4; ++d) col_base[d] = a.packed + tile_index(tile_col(d), 0, a.tiles_k_total, a.tiles_n_total) * kTileBytes;
             int issued = 0;
@@ -215,6 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         // and warps 6-9 columns 128-255.
         const int q = warp & 3, half = dw >> 2;
         const int row = 32 * q + lane, tok = m0 + row;
+        pdl_wait();
         if (ok && mbar_wait(acc_full, 0, abort, status)) {
             fence_after_sync();
             const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * q) << 16) + 128 * half;
@@ -322,8 +325,11 @@ int launch(const CUtensorMap &map, const GemmArgs &a, cudaStream_t stream) {
             configured[dev] = true;
         }
     }
-    dim3 grid((a.m + BM - 1) / BM, a.n_tiles / 4);
-    kernel<<<grid, kThreads, kSmemBytes, stream>>>(map, a);
+    const cudaError_t e = launch_pdl(kernel, dim3((a.m + BM - 1) / BM, a.n_tiles / 4), dim3(kThreads), kSmemBytes, stream, map, a);
+    if (e != cudaSuccess) {
+        set_cuda_error(e);
+        return HMB_ERR_CUDA;
+    }
     return launch_status();
 }
 

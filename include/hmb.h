@@ -166,6 +166,12 @@ int hmb_w4a16_ffn(const uint8_t *gate_up, const uint8_t *down, int64_t h, int64_
                   hmb_stream_t stream);
 size_t hmb_w4a16_ffn_workspace(int64_t m, int64_t h, int64_t n);
 
+/* Self-test of failure detection: launches one warp that waits on an mbarrier nothing arrives on and
+ * gives up after limit_ns (at most 100 ms), exactly as the GEMM and GEMV waits do; afterwards
+ * hmb_device_status reports HMB_ERR_TIMEOUT and the context stays usable. No counterpart in the
+ * reference (its kernels have no bounded waits). */
+int hmb_selftest_bounded_wait(int64_t limit_ns, hmb_stream_t stream);
+
 /* Reads and clears the device status word of the current device: *status = HMB_ERR_TIMEOUT if a kernel
  * gave up a bounded wait since the last call, else HMB_OK. Synchronizes `stream`. */
 int hmb_device_status(int *status, hmb_stream_t stream);
