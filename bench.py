@@ -70,7 +70,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="cfg1", choices=sorted(CONFIGS))
-    ap.add_argument("--m", type=int, default=0, help="tokens per step (default: the workload's)")
+    ap.add_argument("--m", "--tokens", dest="m", type=int, default=0,
+                    help="tokens per step (default: the workload's); --tokens under torchrun")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (testing only)")
     ap.add_argument("--impl", default="hmb", choices=["hmb", "reference"])
     ap.add_argument("--no-graph", action="store_true")
@@ -219,6 +220,8 @@ def run_hmb(args):
             layers.append(H.slice_packed_ffn(g, u, d, h, inter, 0, inter, H.GateUpLayout.kInterleaved))
         del g, u, d
     torch.cuda.synchronize()
+    if tp is not None:
+        tp.connect(m, dev)  # the NVLink boundary-sum buffers, before any capture
     trace("weights ready")
     stack = FfnStack(layers, h, dev, tp=tp)
     n_local = stack.layers[0].channels()
@@ -324,6 +327,8 @@ def run_hmb(args):
         del graph, step
     stack.release()
     if world > 1:
+        dist.barrier(device_ids=[local])
+        tp.close()  # no rank touches a peer's buffers after the barrier
         dist.barrier(device_ids=[local])
         trace("destroying process group")
         dist.destroy_process_group()

@@ -45,6 +45,11 @@ SIGNATURES = {
     "hmb_w4a16_ffn": (_int, [_vp, _vp, _i64, _i64, _i64, _int, _vp, _i64, _int, _vp, _i64, _int, _i64, _vp, _sz, _vp]),
     "hmb_w4a16_ffn_workspace": (_sz, [_i64, _i64, _i64]),
     "hmb_selftest_bounded_wait": (_int, [_i64, _vp]),
+    "hmb_comm_handle_bytes": (_sz, []),
+    "hmb_comm_create": (_int, [_int, _int, _sz, _vp, _vp]),
+    "hmb_comm_connect": (_int, [_vp, _vp]),
+    "hmb_allreduce_partials": (_int, [_vp, _i64, _int, _vp, _vp, ctypes.c_uint64]),
+    "hmb_comm_destroy": (_int, [_vp]),
     "hmb_device_status": (_int, [_vp, _vp]),
     "hmb_silu_mul": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _int, _vp]),
     "hmb_residual_add2": (_int, [_vp, _i64, _vp, _i64, _int, _vp, _i64, _int, _i64, _i64, _vp]),

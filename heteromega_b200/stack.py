@@ -5,7 +5,7 @@ GpuFfnModel::forward). On B200 a decode layer takes a few microseconds, so the p
 launches would dominate; FfnStack captures the whole layer sequence for a given M once and
 replays it. Layer l reads x[l] and writes y[l] ([L, M, H] bf16 buffers that the graph owns).
 With a TensorParallelFfn the layers are this rank's shards and each layer ends with the
-boundary all-reduce (NCCL, captured in the same graph).
+boundary all-reduce (the NVLink peer-memory kernel, captured in the same graph).
 """
 import torch
 
@@ -31,9 +31,9 @@ class FfnStack:
             w: FfnSliceWeights = self.layers[l]
             gpu_ffn_slice_forward(w, x, _Act(act), y)
         else:
-            self.tp.local_partial(l, x, partial, act)
-            self.tp.reduce_partials(partial)
-            y.copy_(partial)
+            # this rank's partial straight into y, then summed over the ranks in place
+            self.tp.local_partial(l, x, y)
+            self.tp.reduce_partials(y)
 
     def forward(self, x_all, y_all, scratch=None):
         """Eager: y_all[l] = FFN_l(x_all[l]) for every layer, on the current stream."""
@@ -46,8 +46,7 @@ class FfnStack:
     def _scratch(self, m):
         n = max(w.channels() for w in self.layers)
         act = torch.empty(m, n, dtype=torch.bfloat16, device=self.device)
-        partial = torch.empty(m, self.hidden, dtype=torch.float32, device=self.device) if self.tp is not None else None
-        return act, partial
+        return act, None
 
     def graph(self, m):
         """(graph, x_all, y_all) for M rows, captured on first use. Fill x_all, replay, read y_all."""

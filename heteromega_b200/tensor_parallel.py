@@ -5,20 +5,66 @@ and a GPU and sums the two partial outputs at the layer boundary
 (src/unified_llm_w4a16_hetero/merged_ffn.cpp:235-236, 417; kernels/gpu/src/residual_add.cu).
 On B200 the devices are P GPUs, one process each: rank r owns channels [b_r, e_r) of every
 layer (partition.plan_shards), gate/up column-parallel (an interleaved gate_up slice) and down
-row-parallel. Each rank computes its partial output in fp32 and one all-reduce (sum) per layer
-over NCCL on the compute stream replaces the reference's boundary sum; the fp32 sum is rounded
-to bf16 once, as residual_add2 does.
+row-parallel. Each rank computes its partial output (bf16, as the reference's GPU partial is) and
+one all-reduce (sum) per layer replaces the reference's boundary sum: on GPUs the library's own
+NVLink peer-memory kernel (hmb_allreduce_partials: fp32 sums in rank order, one rounding, the same
+bits on every rank), NCCL on request, and the process group's all-reduce for CPU tensors (gloo).
 """
+import ctypes
+
 import torch
 import torch.distributed as dist
 
+from . import _lib
+from ._lib import check, lib
 from .gpu_ffn import FfnSliceWeights, GateUpLayout, slice_packed_ffn
 from .partition import plan_shards
 from .torch_ops import ops
 
 
+class PeerComm:
+    """Symmetric NVLink buffers of one process group: every rank allocates its receive slots and flag
+    words, and the CUDA IPC handles are exchanged over the group so that each rank can store into its
+    peers' slots. Messages up to max_bytes."""
+
+    def __init__(self, max_bytes, group=None, device=None):
+        self.group = group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.max_bytes = int(max_bytes)
+        hb = lib().hmb_comm_handle_bytes()
+        handle = (ctypes.c_uint8 * hb)()
+        ptr = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            check(lib().hmb_comm_create(self.rank, self.world, self.max_bytes, ctypes.byref(ptr), handle), "hmb_comm_create")
+        self._ptr = ptr
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        joined = (ctypes.c_uint8 * (hb * self.world)).from_buffer_copy(b"".join(handles))
+        with torch.cuda.device(self.device):
+            check(lib().hmb_comm_connect(self._ptr, joined), "hmb_comm_connect")
+        dist.barrier(group=group, device_ids=[self.device.index])
+
+    def all_reduce(self, t, spin_limit_ns=0):
+        """t (bf16/fp16/fp32, contiguous, on this rank's GPU) = the sum over the ranks, in place."""
+        if not t.is_contiguous() or t.device != self.device:
+            raise ValueError("PeerComm.all_reduce: t must be contiguous on the communicator's device")
+        code = {torch.bfloat16: _lib.HMB_BF16, torch.float16: _lib.HMB_FP16, torch.float32: _lib.HMB_FP32}[t.dtype]
+        check(lib().hmb_allreduce_partials(t.data_ptr(), t.numel(), code, self._ptr,
+                                           torch.cuda.current_stream(t.device).cuda_stream, spin_limit_ns),
+              "hmb_allreduce_partials")
+        return t
+
+    def close(self):
+        if self._ptr is not None:
+            check(lib().hmb_comm_destroy(self._ptr), "hmb_comm_destroy")
+            self._ptr = None
+
+
 class TensorParallelFfn:
-    def __init__(self, hidden, inter, group=None, ratios=None, rank=None, world=None):
+    def __init__(self, hidden, inter, group=None, ratios=None, rank=None, world=None, collective="hmb"):
+        """collective: "hmb" (NVLink peer-memory kernel for CUDA tensors) or "nccl" (the process
+        group's all-reduce); CPU tensors always use the process group."""
         self.group = group
         self.rank = dist.get_rank(group) if rank is None else rank
         self.world = dist.get_world_size(group) if world is None else world
@@ -27,6 +73,10 @@ class TensorParallelFfn:
         self.begin, self.end = self.shares[self.rank]
         self.layers = []
         self._partial = None
+        if collective not in ("hmb", "nccl"):
+            raise ValueError("collective must be 'hmb' or 'nccl'")
+        self.collective = collective
+        self.comm = None
 
     @property
     def channels(self):
@@ -43,13 +93,27 @@ class TensorParallelFfn:
             raise ValueError("add_shard: shard does not match this rank's interleaved channel range")
         self.layers.append(w)
 
-    def partial_buffer(self, m, device):
-        if self._partial is None or self._partial.numel() < m * self.hidden or self._partial.device != device:
-            self._partial = torch.empty(m * self.hidden, dtype=torch.float32, device=device)
+    def partial_buffer(self, m, device, dtype=torch.float32):
+        if (self._partial is None or self._partial.numel() < m * self.hidden or self._partial.device != device
+                or self._partial.dtype != dtype):
+            self._partial = torch.empty(m * self.hidden, dtype=dtype, device=device)
         return self._partial[:m * self.hidden].view(m, self.hidden)
 
+    def connect(self, max_rows, device):
+        """Sets up the NVLink communicator for partials of up to max_rows rows (collective "hmb");
+        every rank of the group must call it."""
+        if self.world > 1 and self.collective == "hmb" and self.comm is None:
+            self.comm = PeerComm(max_rows * self.hidden * 4, self.group, device)
+        return self.comm
+
+    def close(self):
+        if self.comm is not None:
+            self.comm.close()
+            self.comm = None
+
     def local_partial(self, layer, x, partial, act=None):
-        """partial[m, H] (fp32) = this rank's share of FFN layer `layer` for x [m, H] (bf16)."""
+        """partial[m, H] (bf16/fp16, or fp32 for unrounded sums) = this rank's share of FFN layer
+        `layer` for x [m, H]."""
         w = self.layers[layer]
         n, stored, h = w.channels(), w.stored_channels(), w.hidden
         ops.w4a16_ffn(partial, x, w.gate_up, w.down, h, n, stored, int(w.layout))
@@ -57,14 +121,18 @@ class TensorParallelFfn:
 
     def reduce_partials(self, partial):
         """Sum of every rank's partial, in place (one all-reduce)."""
-        if self.world > 1:
-            dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group)
+        if self.world == 1:
+            return partial
+        if partial.is_cuda and self.collective == "hmb":
+            if self.comm is None or partial.numel() * partial.element_size() > self.comm.max_bytes:
+                raise RuntimeError("TensorParallelFfn: call connect(max_rows, device) on every rank first")
+            return self.comm.all_reduce(partial)
+        dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group)
         return partial
 
     def forward(self, layer, x, y):
-        """y[m, H] (bf16) = the whole FFN layer for x, on every rank."""
-        partial = self.partial_buffer(x.shape[0], x.device)
-        self.local_partial(layer, x, partial)
-        self.reduce_partials(partial)
-        y.copy_(partial)
+        """y[m, H] (x's dtype) = the whole FFN layer for x, on every rank: this rank's partial written
+        into y and summed in place."""
+        self.local_partial(layer, x, y)
+        self.reduce_partials(y)
         return y

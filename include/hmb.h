@@ -33,6 +33,7 @@ extern "C" {
 #endif
 
 typedef struct CUstream_st *hmb_stream_t; /* a cudaStream_t */
+typedef struct hmb_comm hmb_comm;         /* opaque: one rank of a tensor-parallel group */
 
 enum { HMB_TILE_K = 128, HMB_TILE_N = 64, HMB_TILE_BYTES = 4352 };
 
@@ -171,6 +172,22 @@ size_t hmb_w4a16_ffn_workspace(int64_t m, int64_t h, int64_t n);
  * hmb_device_status reports HMB_ERR_TIMEOUT and the context stays usable. No counterpart in the
  * reference (its kernels have no bounded waits). */
 int hmb_selftest_bounded_wait(int64_t limit_ns, hmb_stream_t stream);
+
+/* Tensor-parallel boundary sum over NVLink peer memory (the counterpart of the per-layer partial sum:
+ * heteromega::residual_add2, kernels/gpu/src/residual_add.cu:55-73; MergedFfn::add_out,
+ * src/unified_llm_w4a16_hetero/merged_ffn.cpp:417). One communicator per rank of a P-rank group
+ * (P <= 8, one GPU each): hmb_comm_create allocates this rank's receive slots and flag words and
+ * writes its CUDA IPC handle (hmb_comm_handle_bytes bytes); after the handles of all ranks are
+ * exchanged (rank order), hmb_comm_connect opens the peers'. hmb_allreduce_partials then replaces
+ * y (bf16, fp16 or fp32; elems * size a multiple of 16 bytes, at most max_bytes) on every rank by
+ * the sum over the ranks: fp32 sums in rank order, one rounding, the same bits everywhere. Every
+ * rank must make the same calls in the same order. Waits give up after spin_limit_ns (0: one
+ * second) with HMB_ERR_TIMEOUT in the device status word. No multicast: plain stores over NVLink. */
+size_t hmb_comm_handle_bytes(void);
+int hmb_comm_create(int rank, int world, size_t max_bytes, hmb_comm **comm, void *handle);
+int hmb_comm_connect(hmb_comm *comm, const void *handles);
+int hmb_allreduce_partials(void *y, int64_t elems, int dtype, hmb_comm *comm, hmb_stream_t stream, uint64_t spin_limit_ns);
+int hmb_comm_destroy(hmb_comm *comm);
 
 /* Reads and clears the device status word of the current device: *status = HMB_ERR_TIMEOUT if a kernel
  * gave up a bounded wait since the last call, else HMB_OK. Synchronizes `stream`. */

@@ -4,7 +4,8 @@ CPU part (gloo, world size 2): each rank slices its shard out of the whole packe
 slice path, computes its partial output with the CPU oracle, and the all-reduce of the partials must
 give the unsharded FFN — the algebra of npu/ffn/reference.py:200-221 over P ranks. Also checks the
 partition planner against the reference's from_ratio rounding.
-GPU part (NCCL, 2 GPUs): the same through the CUDA kernels; skipped with fewer GPUs.
+GPU part (2 GPUs): the same through the CUDA kernels, with the library's NVLink all-reduce and with
+NCCL; skipped with fewer GPUs.
 """
 import os
 import socket
@@ -102,11 +103,12 @@ def test_gloo_partials_sum_to_full_ffn(tmp_path, inter):
     assert_close(r["got"], r["ref"], (1e-5, 1e-5, 0.9999999), "sum of rank partials")
 
 
-def _nccl_rank(rank, world, port, out_path):
+def _gpu_rank(rank, world, port, out_path, collective):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    tp = None
     try:
         from heteromega_b200.weights import synthetic_packed_device
 
@@ -116,34 +118,52 @@ def _nccl_rank(rank, world, port, out_path):
         g = synthetic_packed_device(hidden, inter, dev, gen)
         u = synthetic_packed_device(hidden, inter, dev, gen)
         d = synthetic_packed_device(inter, hidden, dev, gen)
-        tp = TensorParallelFfn(hidden, inter)
+        tp = TensorParallelFfn(hidden, inter, collective=collective)
         tp.add_layer(g, u, d)
+        tp.connect(1024, dev)
         full = H.slice_packed_ffn(g, u, d, hidden, inter, 0, inter, H.GateUpLayout.kInterleaved)
         res = {}
-        for m in (1, 300):
+        for m in (1, 7, 300, 1024):
             gen.manual_seed(12 + m)
             x = torch.randn(m, hidden, device=dev, generator=gen).to(torch.bfloat16)
             y = torch.empty(m, hidden, dtype=torch.bfloat16, device=dev)
-            tp.forward(0, x, y)
+            for _ in range(3):  # repeated calls: the communicator's epochs and double buffers advance
+                tp.forward(0, x, y)
             ref = torch.empty_like(y)
             H.gpu_ffn_slice_forward(full, x, None, ref)
             torch.cuda.synchronize()
             res[f"got{m}"], res[f"ref{m}"] = y.float().cpu().numpy(), ref.float().cpu().numpy()
-        if rank == 0:
-            np.savez(out_path, **res)
+        # every rank holds the same bits
+        mine = torch.cat([torch.from_numpy(res[f"got{m}"]).flatten() for m in (1, 7, 300, 1024)]).to(dev)
+        other = mine.clone()
+        dist.broadcast(other, src=0)
+        res["same_bits"] = np.array(bool(torch.equal(mine, other)))
+        from heteromega_b200.torch_ops import device_status
+
+        res["status"] = np.array(device_status(dev))
+        np.savez(out_path + f".{rank}.npz", **res)
         dist.barrier(device_ids=[rank])
     finally:
+        if tp is not None:
+            tp.close()
+        dist.barrier(device_ids=[rank])
         dist.destroy_process_group()
 
 
 @pytest.mark.gpu
-def test_nccl_two_gpus(tmp_path):
+@pytest.mark.parametrize("collective", ["hmb", "nccl"])
+def test_two_gpus(tmp_path, collective):
+    """Tensor parallel over 2 GPUs against the single-GPU FFN: the NVLink peer-memory all-reduce (both
+    its one-shot and two-shot sizes) and NCCL; decode and prefill rows."""
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    out = str(tmp_path / "nccl.npz")
-    mp.start_processes(_nccl_rank, args=(2, free_port(), out), nprocs=2, join=True, start_method="spawn")
-    r = np.load(out)
+    out = str(tmp_path / "tp")
+    mp.start_processes(_gpu_rank, args=(2, free_port(), out, collective), nprocs=2, join=True, start_method="spawn")
     from metrics import LEVEL, assert_close
 
-    for m in (1, 300):
-        assert_close(r[f"got{m}"], r[f"ref{m}"], LEVEL, f"TP2 vs single GPU m={m}")
+    for rank in range(2):
+        r = np.load(out + f".{rank}.npz")
+        assert int(r["status"]) == 0
+        assert bool(r["same_bits"])
+        for m in (1, 7, 300, 1024):
+            assert_close(r[f"got{m}"], r[f"ref{m}"], LEVEL, f"TP2 {collective} vs single GPU m={m} rank {rank}")
