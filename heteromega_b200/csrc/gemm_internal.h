@@ -23,7 +23,26 @@ struct PairArgs {
     int col_stride;  // SwiGLU blocked layout: tile columns from gate to up; 1 = interleaved
     int y_f32;       // HMB_EPI_STORE: write the fp32 sums instead of rounding them
     int *status;     // device status word (1 after a wait gave up)
+    int k_splits;    // splits of K per tile (1: none)
+    int k_per_split; // K steps (of 64) per split
+    float *split_ws;      // k_splits > 1: [tile][split][CTA] 128 x 256 fp32 sums
+    unsigned *split_cnt;  // k_splits > 1: [tile][CTA] arrival and completion counters (self-resetting)
 };
+
+// CTA pairs the pair kernel keeps resident on the current device.
+int pair_clusters();
+// K splits for an m x n output with k/64 K steps (1 when the tiles already fill the GPU), and the
+// workspace bytes they need.
+int pair_k_splits(int64_t m, int64_t k, int64_t n);
+size_t pair_split_bytes(int64_t m, int64_t k, int64_t n);
+
+// hmb_w4a16_gemm with an optional split-K workspace: split_ws (pair_split_bytes(m, k, n) bytes of
+// fp32 sums) and split_cnt (4 KB of counters, zero before the first call; the kernel leaves them
+// zero). Without them (nullptr) no K splits are used.
+int gemm_run(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const void *x, int64_t ldx, int x_dtype, void *y, int64_t ldy,
+             int y_dtype, int64_t m, int64_t k, int64_t n, int64_t start_col, int epilogue, int layout, void *split_ws, size_t split_ws_bytes,
+             unsigned *split_cnt, cudaStream_t stream);
+constexpr size_t kSplitCounterBytes = 4096;
 
 // Launches the CTA-pair kernel; `map` is x as a 2D tensor map with 64 x 128 boxes (SWIZZLE_128B).
 int launch_gemm_pair(const CUtensorMap &map, const PairArgs &a, bool f16, int epilogue, cudaStream_t stream);

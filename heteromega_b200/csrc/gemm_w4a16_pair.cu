@@ -69,6 +69,123 @@ constexpr int kTmemCols = 256 * kAccStages;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory plan");
 static_assert(kBOff % 1024 == 0 && kPOff % 1024 == 0, "stage alignment");
 
+// Epilogue of one split of a split-K tile, run by the 4 epilogue warps of a CTA (thread = row
+// 32 q + lane of this CTA's 128 rows). The split's fp32 sums go to its slot of the workspace and the
+// accumulator is released; the splits of the tile meet at a counter (all of them are resident); then
+// each split adds the slots, in split order, for its share of the rows and writes the outputs.
+template <bool F16, int EPI>
+__device__ __forceinline__ void split_epilogue(const PairArgs &a, uint32_t taddr, int unit, int tile, int mb, int nb, int rank,
+                                               int q, int lane, volatile int *abort, uint32_t release_bar) {
+    const int S = a.k_splits, ks = unit % S, row = 32 * q + lane;
+    constexpr int kRowFloats = 256, kSlotFloats = 128 * kRowFloats;
+    float *part = a.split_ws + (static_cast<int64_t>(tile * S + ks) * 2 + rank) * kSlotFloats;
+    for (int cb = 0; cb < 8; ++cb) {
+        uint32_t v[32];
+        tmem_ld32(taddr + 32 * cb, v);
+        float *dst = part + row * kRowFloats + 32 * cb;
+#pragma unroll
+        for (int g8 = 0; g8 < 4; ++g8) {
+            float o[8];
+#pragma unroll
+            for (int p = 0; p < 8; ++p) o[p] = __uint_as_float(v[8 * g8 + perm_pos(p)]);
+            __stcg(reinterpret_cast<float4 *>(dst + 8 * g8), make_float4(o[0], o[1], o[2], o[3]));
+            __stcg(reinterpret_cast<float4 *>(dst + 8 * g8 + 4), make_float4(o[4], o[5], o[6], o[7]));
+        }
+    }
+    fence_before_sync();
+    __syncwarp();
+    if (lane == 0) mbar_arrive_cluster(release_bar);  // the accumulator is free
+    unsigned *cnt = a.split_cnt + 2 * (tile * 2 + rank);
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (q == 0 && lane == 0) {
+        __threadfence();
+        atomicAdd(cnt, 1u);
+        const uint64_t start = global_ns();
+        for (uint32_t i = 0;; ++i) {
+            unsigned c;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(c) : "l"(cnt) : "memory");
+            if (static_cast<int>(c) >= S) break;
+            if ((i & 15) == 15 && (*abort || global_ns() - start > kWaitLimitNs)) {
+                *abort = 1;
+                atomicOr(a.status, 1);
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (!*abort) {
+        // This split's rows [r0, r1) of the CTA's 128; work items of 8 outputs, spread over 128 threads.
+        const int r0 = 128 * ks / S, r1 = 128 * (ks + 1) / S;
+        const float *slot0 = a.split_ws + (static_cast<int64_t>(tile * S) * 2 + rank) * kSlotFloats;
+        const int64_t split_stride = 2 * static_cast<int64_t>(kSlotFloats);
+        constexpr int kItemsPerRow = EPI == HMB_EPI_SWIGLU ? 16 : 32;  // 128 channels or 256 columns, 8 each
+        for (int item = row; item < (r1 - r0) * kItemsPerRow; item += 128) {
+            const int rr = r0 + item / kItemsPerRow, c8 = item % kItemsPerRow;
+            const int tk = 256 * mb + 128 * rank + rr;
+            if (tk >= a.m) continue;
+            if constexpr (EPI == HMB_EPI_SWIGLU) {
+                // channels 8 c8 .. + 7 of block pair chb = c8 / 8: gate columns 128 chb + 8 (c8 % 8), up + 64
+                const int chb = c8 >> 3, j8 = c8 & 7;
+                const int gc = 128 * chb + 8 * j8;
+                float g[8], u[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) g[e] = u[e] = 0.0f;
+                for (int sp = 0; sp < S; ++sp) {
+                    const float *src = slot0 + sp * split_stride + rr * kRowFloats;
+                    const float4 g0 = __ldcg(reinterpret_cast<const float4 *>(src + gc));
+                    const float4 g1 = __ldcg(reinterpret_cast<const float4 *>(src + gc + 4));
+                    const float4 u0 = __ldcg(reinterpret_cast<const float4 *>(src + gc + 64));
+                    const float4 u1 = __ldcg(reinterpret_cast<const float4 *>(src + gc + 68));
+                    g[0] += g0.x; g[1] += g0.y; g[2] += g0.z; g[3] += g0.w; g[4] += g1.x; g[5] += g1.y; g[6] += g1.z; g[7] += g1.w;
+                    u[0] += u0.x; u[1] += u0.y; u[2] += u0.z; u[3] += u0.w; u[4] += u1.x; u[5] += u1.y; u[6] += u1.z; u[7] += u1.w;
+                }
+                uint32_t o[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    uint32_t pr = 0;
+#pragma unroll
+                    for (int hl = 0; hl < 2; ++hl) {
+                        const float gg = round16<F16>(g[2 * e + hl]), uu = round16<F16>(u[2 * e + hl]);
+                        pr |= to16<F16>(gg / (1.0f + __expf(-gg)) * uu) << (16 * hl);
+                    }
+                    o[e] = pr;
+                }
+                uint16_t *y = static_cast<uint16_t *>(a.y) + static_cast<int64_t>(tk) * a.ldy + (2 * nb + chb) * kTileN + 8 * j8;
+                *reinterpret_cast<uint4 *>(y) = make_uint4(o[0], o[1], o[2], o[3]);
+            } else {
+                float acc8[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc8[e] = 0.0f;
+                for (int sp = 0; sp < S; ++sp) {
+                    const float *src = slot0 + sp * split_stride + rr * kRowFloats + 8 * c8;
+                    const float4 v0 = __ldcg(reinterpret_cast<const float4 *>(src));
+                    const float4 v1 = __ldcg(reinterpret_cast<const float4 *>(src + 4));
+                    acc8[0] += v0.x; acc8[1] += v0.y; acc8[2] += v0.z; acc8[3] += v0.w;
+                    acc8[4] += v1.x; acc8[5] += v1.y; acc8[6] += v1.z; acc8[7] += v1.w;
+                }
+                if (a.y_f32) {
+                    float *y = static_cast<float *>(a.y) + static_cast<int64_t>(tk) * a.ldy + nb * 256 + 8 * c8;
+                    *reinterpret_cast<float4 *>(y) = make_float4(acc8[0], acc8[1], acc8[2], acc8[3]);
+                    *reinterpret_cast<float4 *>(y + 4) = make_float4(acc8[4], acc8[5], acc8[6], acc8[7]);
+                } else {
+                    uint32_t o[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) o[e] = to16<F16>(acc8[2 * e]) | (to16<F16>(acc8[2 * e + 1]) << 16);
+                    uint16_t *y = static_cast<uint16_t *>(a.y) + static_cast<int64_t>(tk) * a.ldy + nb * 256 + 8 * c8;
+                    *reinterpret_cast<uint4 *>(y) = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+            }
+        }
+    }
+    // The last split to finish resets the tile's counters for the next call.
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (q == 0 && lane == 0 && atomicAdd(cnt + 1, 1u) == static_cast<unsigned>(S - 1)) {
+        atomicExch(cnt, 0u);
+        atomicExch(cnt + 1, 0u);
+    }
+}
+
 template <bool F16, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const PairArgs a) {
@@ -93,6 +210,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool leader = rank == 0;
     const int cluster = static_cast<int>(cluster_id_x()), nclusters = static_cast<int>(nclusters_x());
     const int num_k = 2 * a.k_tiles;
+    // Work unit u = (tile u / k_splits, K steps [k0, k1) of split u % k_splits). With k_splits > 1 all
+    // units are resident at once (units <= clusters), and the splits of a tile add up in the epilogue.
+    const int num_units = a.num_tiles * a.k_splits;
+    auto unit_k0 = [&](int u) { return (u % a.k_splits) * a.k_per_split; };
+    auto unit_k1 = [&](int u) { return min(num_k, unit_k0(u) + a.k_per_split); };
     // Tile t -> (row block, column block): the operand that is larger in bytes stays resident in L2
     // while the other one streams (column blocks fastest when x is the larger one).
     auto tile_mb = [&](int t) { return a.cols_fastest ? t / a.n_blocks : t % a.m_blocks; };
@@ -143,10 +265,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             pdl_wait();
             int it = 0;
             bool ok = true;
-            for (int tile = cluster; ok && tile < a.num_tiles; tile += nclusters) {
-                const int mb = tile_mb(tile);
+            for (int unit = cluster; ok && unit < num_units; unit += nclusters) {
+                const int mb = tile_mb(unit / a.k_splits);
                 const int row0 = 256 * mb + 128 * static_cast<int>(rank);
-                for (int i = 0; i < num_k; ++i, ++it) {
+                for (int i = unit_k0(unit); i < unit_k1(unit); ++i, ++it) {
                     const int s = it % kXStages, u = it / kXStages;
                     if (u > 0 && !mbar_wait(done(s), (u - 1) & 1, abort, a.status)) {
                         ok = false;
@@ -163,12 +285,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             int it = 0;
             bool ok = true;
-            for (int tile = cluster; ok && tile < a.num_tiles; tile += nclusters) {
-                const int nb = tile_nb(tile);
+            for (int unit = cluster; ok && unit < num_units; unit += nclusters) {
+                const int nb = tile_nb(unit / a.k_splits);
                 const uint8_t *col_base[2];
                 for (int d = 0; d < 2; ++d)
                     col_base[d] = a.packed + tile_index(tile_col(nb, 2 * static_cast<int>(rank) + d), 0, a.tiles_k_total, a.tiles_n_total) * kTileBytes;
-                for (int i = 0; i < num_k; ++i, ++it) {
+                for (int i = unit_k0(unit); i < unit_k1(unit); ++i, ++it) {
                     const int s = it % kPStages, u = it / kPStages;
                     if (u > 0 && !mbar_wait(empty_p(s), (u - 1) & 1, abort, a.status)) {
                         ok = false;
@@ -196,12 +318,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             constexpr uint32_t a_hi = smem_desc_hi(1024), b_hi = smem_desc_hi(2048);
             int it = 0, t = 0;
             bool ok = true;
-            for (int tile = cluster; ok && tile < a.num_tiles; tile += nclusters, ++t) {
+            for (int unit = cluster; ok && unit < num_units; unit += nclusters, ++t) {
                 const int acc = t % kAccStages, ua = t / kAccStages;
+                const int k0 = unit_k0(unit);
                 if (ua > 0 && !mbar_wait(tmem_empty(acc), (ua - 1) & 1, abort, a.status)) break;
                 fence_after_sync();
                 const uint32_t d = tmem + 256 * acc;
-                for (int i = 0; i < num_k; ++i, ++it) {
+                for (int i = k0; i < unit_k1(unit); ++i, ++it) {
                     const int sx = it % kXStages, sb = it % kBStages;
                     // full_b implies full_x: the even CTA's dequant warps wait for both CTAs' x tiles
                     // before they arrive.
@@ -213,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t a_lo = a_lo0 + sx * (kXBytes >> 4), b_lo = b_lo0 + sb * (kBBytes >> 4);
 #pragma unroll
                     for (int kk = 0; kk < BK / 16; ++kk)
-                        umma_f16_pair_lohi(d, a_lo + kk * 2, a_hi, b_lo + kk * 256, b_hi, idesc, (i | kk) != 0);
+                        umma_f16_pair_lohi(d, a_lo + kk * 2, a_hi, b_lo + kk * 256, b_hi, idesc, i != k0 || kk != 0);
                     umma_commit_pair(done(sx), 3);
                 }
                 if (ok) umma_commit_pair(tmem_full(acc), 3);
@@ -243,8 +366,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ld_off = dl * kPHalf + 16 * lane + 512 * c0;
         int it = 0;
         bool ok = true;
-        for (int tile = cluster; ok && tile < a.num_tiles; tile += nclusters) {
-            for (int i = 0; i < num_k; ++i, ++it) {
+        for (int unit = cluster; ok && unit < num_units; unit += nclusters) {
+            for (int i = unit_k0(unit); i < unit_k1(unit); ++i, ++it) {
                 if (it % kDqGroups != g) continue;
                 const int s = it % kPStages, sb = it % kBStages, jb = it - kBStages;
                 if (!mbar_wait(full_p(s), (it / kPStages) & 1, abort, a.status) ||
@@ -280,13 +403,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int q = warp & 3;
         pdl_wait();
         int t = 0;
-        for (int tile = cluster; tile < a.num_tiles; tile += nclusters, ++t) {
+        for (int unit = cluster; unit < num_units; unit += nclusters, ++t) {
             const int acc = t % kAccStages;
             if (!mbar_wait(tmem_full(acc), (t / kAccStages) & 1, abort, a.status)) break;
             fence_after_sync();
+            const int tile = unit / a.k_splits;
             const int mb = tile_mb(tile), nb = tile_nb(tile);
             const int tok = 256 * mb + 128 * static_cast<int>(rank) + 32 * q + lane;
             const uint32_t taddr = tmem + 256 * acc + (static_cast<uint32_t>(32 * q) << 16);
+            if (a.k_splits > 1) {
+                split_epilogue<F16, EPI>(a, taddr, unit, tile, mb, nb, static_cast<int>(rank), q, lane, abort,
+                                         mapa(tmem_empty(acc), 0));
+                continue;
+            }
             if constexpr (EPI == HMB_EPI_SWIGLU) {
                 for (int ch = 0; ch < 2; ++ch) {
                     // Block pair ch: gate = columns 128 ch .. + 63, up = 128 ch + 64 .. + 127.
@@ -364,10 +493,23 @@ template <bool F16, int EPI>
 int launch(const CUtensorMap &map, const PairArgs &a, cudaStream_t stream) {
     auto kernel = gemm_pair_kernel<F16, EPI>;
     static std::mutex mu;
-    static int max_clusters[64] = {};
+    static bool configured[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 64) return HMB_ERR_UNSUPPORTED;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!configured[dev]) {
+            const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+            if (e != cudaSuccess) {
+                set_cuda_error(e);
+                return HMB_ERR_CUDA;
+            }
+            configured[dev] = true;
+        }
+    }
+    const int max_clusters = pair_clusters();
+    if (max_clusters <= 0) return HMB_ERR_CUDA;
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -380,26 +522,9 @@ int launch(const CUtensorMap &map, const PairArgs &a, cudaStream_t stream) {
     cfg.dynamicSmemBytes = kSmemBytes;
     cfg.stream = stream;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;  // the occupancy query takes the cluster shape only
-    {
-        std::lock_guard<std::mutex> lock(mu);
-        if (max_clusters[dev] == 0) {
-            cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-            int n = 0;
-            if (e == cudaSuccess) {
-                cfg.gridDim = dim3(2 * sm_count());
-                e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
-            }
-            if (e != cudaSuccess || n <= 0) {
-                set_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidConfiguration);
-                return HMB_ERR_CUDA;
-            }
-            max_clusters[dev] = n;
-        }
-    }
-    const int clusters = std::min(a.num_tiles, max_clusters[dev]);
-    cfg.gridDim = dim3(2 * clusters);
     cfg.numAttrs = 2;
+    const int clusters = std::min(a.num_tiles * a.k_splits, max_clusters);
+    cfg.gridDim = dim3(2 * clusters);
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, map, a);
     if (e != cudaSuccess) {
         set_cuda_error(e);
@@ -409,6 +534,52 @@ int launch(const CUtensorMap &map, const PairArgs &a, cudaStream_t stream) {
 }
 
 }  // namespace
+
+int pair_clusters() {
+    static std::mutex mu;
+    static int n_clusters[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return 0;
+    std::lock_guard<std::mutex> lock(mu);
+    if (n_clusters[dev] == 0) {
+        // Every instantiation has the same resources; ask for one of them.
+        auto kernel = gemm_pair_kernel<false, HMB_EPI_STORE>;
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(2 * sm_count());
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = kSmemBytes;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+        if (e != cudaSuccess || n <= 0) {
+            set_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidConfiguration);
+            return 0;
+        }
+        n_clusters[dev] = n;
+    }
+    return n_clusters[dev];
+}
+
+int pair_k_splits(int64_t m, int64_t k, int64_t n) {
+    const int64_t tiles = (m + 255) / 256 * (n / 256), steps = k / BK;
+    const int clusters = pair_clusters();
+    if (tiles <= 0 || clusters <= 0 || 2 * tiles > clusters || steps < 16) return 1;
+    return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(clusters / tiles, steps / 8)));
+}
+
+size_t pair_split_bytes(int64_t m, int64_t k, int64_t n) {
+    const int splits = pair_k_splits(m, k, n);
+    if (splits <= 1) return 0;
+    const int64_t tiles = (m + 255) / 256 * (n / 256);
+    return static_cast<size_t>(tiles * splits * 2) * 128 * 256 * sizeof(float) + static_cast<size_t>(tiles * 2 * 2) * 4 + 256;
+}
 
 int launch_gemm_pair(const CUtensorMap &map, const PairArgs &a, bool f16, int epilogue, cudaStream_t stream) {
     if (f16) return epilogue == HMB_EPI_SWIGLU ? launch<true, HMB_EPI_SWIGLU>(map, a, stream) : launch<true, HMB_EPI_STORE>(map, a, stream);

@@ -349,20 +349,9 @@ int *device_status_word() {
     return addr[dev];
 }
 
-}  // namespace hmb
-
-using namespace hmb;
-
-extern "C" {
-
-int hmb_w4a16_gemm_supports(int64_t m, int64_t k, int64_t n, int epilogue) {
-    if (m <= 0 || k <= 0 || n <= 0 || k % kTileK) return 0;
-    return n % BN == 0 && (epilogue == HMB_EPI_STORE || epilogue == HMB_EPI_SWIGLU) && m < (int64_t(1) << 30);
-}
-
-int hmb_w4a16_gemm(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const void *x, int64_t ldx, int x_dtype, void *y,
-                   int64_t ldy, int y_dtype, int64_t m, int64_t k, int64_t n, int64_t start_col, int epilogue, int layout,
-                   hmb_stream_t stream) {
+int gemm_run(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const void *x, int64_t ldx, int x_dtype, void *y, int64_t ldy,
+             int y_dtype, int64_t m, int64_t k, int64_t n, int64_t start_col, int epilogue, int layout, void *split_ws, size_t split_ws_bytes,
+             unsigned *split_cnt, cudaStream_t stream) {
     if (!packed || !x || !y || m <= 0) return HMB_ERR_ARG;
     if (k <= 0 || n <= 0 || k % kTileK || n % kTileN || packed_k % kTileK || packed_n % kTileN || start_col < 0 ||
         start_col % kTileN || k > packed_k || start_col + n > packed_n)
@@ -395,7 +384,12 @@ int hmb_w4a16_gemm(const uint8_t *packed, int64_t packed_k, int64_t packed_n, co
 
     const int col_stride = (epilogue == HMB_EPI_SWIGLU && layout == HMB_GATE_UP_BLOCKED) ? static_cast<int>(n / kTileN / 2) : 1;
     const bool f16 = x_dtype == HMB_FP16, swiglu = epilogue == HMB_EPI_SWIGLU;
-    if (m > BM) {
+    // CTA pairs for m > 128, and for smaller m when K splits (which need the caller's workspace) can
+    // fill a GPU that one-CTA tiles would leave mostly idle.
+    const int splits = split_ws && split_cnt ? pair_k_splits(m, k, n) : 1;
+    const bool split_ok = splits > 1 && split_ws_bytes >= pair_split_bytes(m, k, n);
+    const bool small_grid = (m + BM - 1) / BM * (n / BN) * 2 < sm_count();
+    if (m > BM || (split_ok && small_grid)) {
         PairArgs p{};
         p.packed = packed;
         p.y = y;
@@ -412,6 +406,12 @@ int hmb_w4a16_gemm(const uint8_t *packed, int64_t packed_k, int64_t packed_n, co
         p.col_stride = col_stride;
         p.y_f32 = y_dtype == HMB_FP32;
         p.status = status;
+        p.k_splits = split_ok ? splits : 1;
+        const int steps = static_cast<int>(k / BK);
+        p.k_per_split = ((steps + p.k_splits - 1) / p.k_splits + 1) / 2 * 2;
+        p.k_splits = (steps + p.k_per_split - 1) / p.k_per_split;  // no empty split
+        p.split_ws = static_cast<float *>(split_ws);
+        p.split_cnt = split_cnt;
         return launch_gemm_pair(map, p, f16, epilogue, stream);
     }
     GemmArgs a{};
@@ -428,6 +428,24 @@ int hmb_w4a16_gemm(const uint8_t *packed, int64_t packed_k, int64_t packed_n, co
     a.y_f32 = y_dtype == HMB_FP32;
     if (f16) return swiglu ? launch<true, HMB_EPI_SWIGLU>(map, a, stream) : launch<true, HMB_EPI_STORE>(map, a, stream);
     return swiglu ? launch<false, HMB_EPI_SWIGLU>(map, a, stream) : launch<false, HMB_EPI_STORE>(map, a, stream);
+}
+
+}  // namespace hmb
+
+using namespace hmb;
+
+extern "C" {
+
+int hmb_w4a16_gemm_supports(int64_t m, int64_t k, int64_t n, int epilogue) {
+    if (m <= 0 || k <= 0 || n <= 0 || k % kTileK) return 0;
+    return n % BN == 0 && (epilogue == HMB_EPI_STORE || epilogue == HMB_EPI_SWIGLU) && m < (int64_t(1) << 30);
+}
+
+int hmb_w4a16_gemm(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const void *x, int64_t ldx, int x_dtype, void *y,
+                   int64_t ldy, int y_dtype, int64_t m, int64_t k, int64_t n, int64_t start_col, int epilogue, int layout,
+                   hmb_stream_t stream) {
+    return gemm_run(packed, packed_k, packed_n, x, ldx, x_dtype, y, ldy, y_dtype, m, k, n, start_col, epilogue, layout, nullptr, 0,
+                    nullptr, static_cast<cudaStream_t>(stream));
 }
 
 int hmb_device_status(int *status, hmb_stream_t stream) {

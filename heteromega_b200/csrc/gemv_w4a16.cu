@@ -36,6 +36,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "gemm_internal.h"
 
 namespace hmb {
 namespace {
@@ -654,9 +655,12 @@ int gemv_args(GemvArgs &a, size_t &partial, const uint8_t *packed, int64_t packe
     return HMB_OK;
 }
 
-// Workspace of hmb_w4a16_ffn: [gate/up counters][down counters][act][gate/up slots][down slots]. The
-// prefill (GEMM) path uses act only; the counters stay zero for the decode path.
+// Workspace of hmb_w4a16_ffn: [gate/up GEMV counters][down GEMV counters][gate/up GEMM split counters]
+// [down GEMM split counters][act][scratch]. Counters are never written by another path (each is left
+// zero by its own); the scratch holds the GEMV contributor slots on the decode path and the GEMMs'
+// split-K sums on the prefill path (gate/up and down run one after the other, so they share it).
 size_t round256(size_t b) { return (b + 255) / 256 * 256; }
+constexpr size_t kFfnControlBytes = 2 * kCounterBytes + 2 * kSplitCounterBytes;
 
 }  // namespace
 }  // namespace hmb
@@ -701,9 +705,11 @@ size_t hmb_w4a16_ffn_workspace(int64_t m, int64_t h, int64_t n) {
     if (m <= 0 || h <= 0 || n <= 0 || h % kTileK || n % kTileK) return 0;
     const int64_t rows = std::min<int64_t>(m, 16);
     const int64_t gu_items = (2 * n / kTileN) * (h / kTileK), dn_items = (h / kTileN) * (n / kTileK);
-    return 2 * kCounterBytes + round256(static_cast<size_t>(m) * n * 2) +
-           round256(partial_bytes(rows, n / kTileN, 2, grid_warps(gu_items, 0, rows))) +
-           round256(partial_bytes(rows, h / kTileN, 1, grid_warps(dn_items, 0, rows)));
+    const size_t decode = round256(partial_bytes(rows, n / kTileN, 2, grid_warps(gu_items, 0, rows))) +
+                          round256(partial_bytes(rows, h / kTileN, 1, grid_warps(dn_items, 0, rows)));
+    size_t prefill = 0;
+    if (m > 16) prefill = std::max(pair_split_bytes(m, h, 2 * n), pair_split_bytes(m, n, h));
+    return kFfnControlBytes + round256(static_cast<size_t>(m) * n * 2) + std::max(decode, prefill);
 }
 
 int hmb_w4a16_ffn(const uint8_t *gate_up, const uint8_t *down, int64_t h, int64_t n, int64_t stored, int layout, const void *x,
@@ -715,15 +721,22 @@ int hmb_w4a16_ffn(const uint8_t *gate_up, const uint8_t *down, int64_t h, int64_
     if (!aligned(x, 16) || !aligned(y, 16) || !workspace || !aligned(workspace, 256)) return workspace ? HMB_ERR_ALIGN : HMB_ERR_WORKSPACE;
     if (workspace_bytes < hmb_w4a16_ffn_workspace(m, h, n)) return HMB_ERR_WORKSPACE;
     uint8_t *ws = static_cast<uint8_t *>(workspace);
-    const size_t act_off = 2 * kCounterBytes;
+    unsigned *gu_split_cnt = reinterpret_cast<unsigned *>(ws + 2 * kCounterBytes);
+    unsigned *dn_split_cnt = reinterpret_cast<unsigned *>(ws + 2 * kCounterBytes + kSplitCounterBytes);
+    uint8_t *act_p = ws + kFfnControlBytes;
+    uint8_t *scratch = act_p + round256(static_cast<size_t>(m) * n * 2);
+    const size_t scratch_bytes = workspace_bytes - (scratch - ws);
 
-    // Prefill: the tcgen05 GEMMs, gate/up with the SwiGLU epilogue into act, then down.
+    // Prefill: the tcgen05 GEMMs (K split where the tiles alone would leave the GPU idle), gate/up with
+    // the SwiGLU epilogue into act, then down.
     const bool same_up = layout == HMB_GATE_UP_INTERLEAVED || n == stored;
     if (m > 16 && same_up && hmb_w4a16_gemm_supports(m, h, 2 * n, HMB_EPI_SWIGLU) && hmb_w4a16_gemm_supports(m, n, h, HMB_EPI_STORE)) {
-        void *act = ws + act_off;
-        int rc = hmb_w4a16_gemm(gate_up, h, 2 * stored, x, ldx, x_dtype, act, n, x_dtype, m, h, 2 * n, 0, HMB_EPI_SWIGLU, layout, stream);
+        const cudaStream_t s = static_cast<cudaStream_t>(stream);
+        int rc = gemm_run(gate_up, h, 2 * stored, x, ldx, x_dtype, act_p, n, x_dtype, m, h, 2 * n, 0, HMB_EPI_SWIGLU, layout, scratch,
+                          scratch_bytes, gu_split_cnt, s);
         if (rc != HMB_OK) return rc;
-        return hmb_w4a16_gemm(down, stored, h, act, n, x_dtype, y, ldy, y_dtype, m, n, h, 0, HMB_EPI_STORE, 0, stream);
+        return gemm_run(down, stored, h, act_p, n, x_dtype, y, ldy, y_dtype, m, n, h, 0, HMB_EPI_STORE, 0, scratch, scratch_bytes,
+                        dn_split_cnt, s);
     }
 
     // Decode: the gate/up GEMV with the SwiGLU epilogue into act, then the down GEMV, per 16 rows. The
@@ -735,16 +748,11 @@ int hmb_w4a16_ffn(const uint8_t *gate_up, const uint8_t *down, int64_t h, int64_
     if (rc != HMB_OK) return rc;
     rc = gemv_args(dn, dn_partial, down, stored, h, n, x_dtype, ldy, y_dtype, m, n, h, 0, HMB_EPI_STORE, 0, 0, 0);
     if (rc != HMB_OK) return rc;
-    size_t off = 0;
-    gu.counters = reinterpret_cast<int *>(ws + off);
-    off += kCounterBytes;
-    dn.counters = reinterpret_cast<int *>(ws + off);
-    off += kCounterBytes;
-    uint16_t *act = reinterpret_cast<uint16_t *>(ws + off);
-    off += round256(static_cast<size_t>(m) * n * 2);
-    gu.partial = reinterpret_cast<float *>(ws + off);
-    off += round256(gu_partial);
-    dn.partial = reinterpret_cast<float *>(ws + off);
+    gu.counters = reinterpret_cast<int *>(ws);
+    dn.counters = reinterpret_cast<int *>(ws + kCounterBytes);
+    uint16_t *act = reinterpret_cast<uint16_t *>(act_p);
+    gu.partial = reinterpret_cast<float *>(scratch);
+    dn.partial = reinterpret_cast<float *>(scratch + round256(gu_partial));
     const size_t y_elem = y_dtype == HMB_FP32 ? 4 : 2;
     for (int64_t r0 = 0; r0 < m; r0 += 16) {
         gu.m = dn.m = static_cast<int>(std::min<int64_t>(16, m - r0));

@@ -110,10 +110,11 @@ def test_gemm_rejects_unsupported_width(cuda, oracle):
         ops.w4a16_gemm(y, x, p, 128, 192, 128, 192, 0, 0, 0)
 
 
-@pytest.mark.parametrize("m", [128, 2048])
+@pytest.mark.parametrize("m", [64, 128, 256, 512, 2048])
 def test_prefill_ffn_layer_sampled_rows(cuda, oracle, m):
     """The Llama-3.2-1B FFN layer at prefill sizes through gpu_ffn_slice_forward (GEMM
-    path), checked on sampled rows against the oracle FFN."""
+    path; K split across CTA pairs where the output tiles alone would leave the GPU idle: the down
+    projection below M=2048, gate/up at M=64), checked on sampled rows against the oracle FFN."""
     hidden, inter = 2048, 8192
     gen = torch.Generator(device=cuda)
     gen.manual_seed(1000)
