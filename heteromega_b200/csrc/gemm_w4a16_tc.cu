@@ -389,7 +389,9 @@ int gemm_run(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const vo
     const int splits = split_ws && split_cnt ? pair_k_splits(m, k, n) : 1;
     const bool split_ok = splits > 1 && split_ws_bytes >= pair_split_bytes(m, k, n);
     const bool small_grid = (m + BM - 1) / BM * (n / BN) * 2 < sm_count();
-    if (m > BM || (split_ok && small_grid)) {
+    // or when the pair tiles fit in one round: two SMs per tile, each dequantizing half of it
+    const bool one_round = (m + 255) / 256 * (n / 256) <= pair_clusters();
+    if (m > BM || (split_ok && small_grid) || (small_grid && one_round)) {
         PairArgs p{};
         p.packed = packed;
         p.y = y;

@@ -22,6 +22,7 @@ class FfnStack:
         self.tp = tp
         self.layers = list(tp.layers) if tp is not None else list(layers)
         self._graphs = {}
+        self._copy_streams = None
 
     def __len__(self):
         return len(self.layers)
@@ -48,9 +49,10 @@ class FfnStack:
         act = torch.empty(m, n, dtype=torch.bfloat16, device=self.device)
         return act, None
 
-    def graph(self, m):
-        """(graph, x_all, y_all) for M rows, captured on first use. Fill x_all, replay, read y_all."""
-        g = self._graphs.get(m)
+    def graph(self, m, slot=0):
+        """(graph, x_all, y_all) for M rows, captured on first use (`slot` > 0: another graph with its
+        own buffers). Fill x_all, replay, read y_all."""
+        g = self._graphs.get((m, slot))
         if g is None:
             L = len(self.layers)
             x_all = torch.zeros(L, m, self.hidden, dtype=torch.bfloat16, device=self.device)
@@ -67,16 +69,56 @@ class FfnStack:
             with torch.cuda.graph(graph, capture_error_mode="thread_local"):
                 self.forward(x_all, y_all, scratch)
             g = (graph, x_all, y_all, scratch)
-            self._graphs[m] = g
+            self._graphs[(m, slot)] = g
         return g[0], g[1], g[2]
 
-    def forward_host(self, x_host, y_host):
-        """The user-facing call with host buffers: copies x_host [L, M, H] (pinned bf16) in, replays
-        the stack, copies y_host out, all on the current stream (no synchronization)."""
-        graph, x_all, y_all = self.graph(x_host.shape[1])
-        x_all.copy_(x_host, non_blocking=True)
-        graph.replay()
-        y_host.copy_(y_all, non_blocking=True)
+    def forward_host(self, x_host, y_host, chunks=None):
+        """The user-facing call with host buffers: x_host [L, M, H] (pinned bf16) in, y_host out; no
+        synchronization, the current stream sees the whole step. From M = 512 the rows go in two
+        chunks, each with its own graph and buffers, so the host-to-device copy of the second chunk
+        and the device-to-host copy of the first overlap the compute (copies on two side streams,
+        ordered by events)."""
+        L, M, _ = x_host.shape
+        if chunks is None:
+            chunks = 2 if M >= 512 else 1
+        cur = torch.cuda.current_stream(self.device)
+        if chunks == 1:
+            graph, x_all, y_all = self.graph(M)
+            x_all.copy_(x_host, non_blocking=True)
+            graph.replay()
+            y_host.copy_(y_all, non_blocking=True)
+            return y_host
+        if self._copy_streams is None:
+            self._copy_streams = (torch.cuda.Stream(self.device), torch.cuda.Stream(self.device))
+        h2d, d2h = self._copy_streams
+        h2d.wait_stream(cur)
+        d2h.wait_stream(cur)
+        computed, copied_out = [None, None], [None, None]
+        for c in range(chunks):
+            r0, r1 = c * M // chunks, (c + 1) * M // chunks
+            slot = c % 2
+            graph, xb, yb = self.graph(r1 - r0, slot)
+            if computed[slot] is not None:
+                h2d.wait_event(computed[slot])  # the slot's x buffer is free again
+            with torch.cuda.stream(h2d):
+                for l in range(L):
+                    xb[l].copy_(x_host[l, r0:r1], non_blocking=True)
+            arrived = torch.cuda.Event()
+            arrived.record(h2d)
+            cur.wait_event(arrived)
+            if copied_out[slot] is not None:
+                cur.wait_event(copied_out[slot])  # the slot's y buffer has been read out
+            graph.replay()
+            computed[slot] = torch.cuda.Event()
+            computed[slot].record(cur)
+            d2h.wait_event(computed[slot])
+            with torch.cuda.stream(d2h):
+                for l in range(L):
+                    y_host[l, r0:r1].copy_(yb[l], non_blocking=True)
+            copied_out[slot] = torch.cuda.Event()
+            copied_out[slot].record(d2h)
+        cur.wait_stream(h2d)
+        cur.wait_stream(d2h)
         return y_host
 
     def kernels_per_step(self):
