@@ -365,7 +365,10 @@ def dominant_kernel(stack, w, x, flush, stream, m, reps=20):
     ms = statistics.median(times)
     from heteromega_b200.torch_ops import GEMV_MAX_ROWS
 
-    return {"name": "gemv_kernel<swiglu> (gate/up + SiLU*up)" if m <= GEMV_MAX_ROWS else "gemm_kernel<swiglu> (tcgen05 gate/up + SiLU*up)",
+    name = ("gemv_kernel<swiglu> (gate/up + SiLU*up)" if m <= GEMV_MAX_ROWS else
+            "gemm_pair_kernel<swiglu> (CTA-pair tcgen05 gate/up + SiLU*up)" if m > 128 else
+            "tcgen05 gate/up + SiLU*up (gemm_kernel or gemm_pair_kernel by shape)")
+    return {"name": name,
             "ms": ms,
             "bytes": h * 2 * n * BYTES_PER_WEIGHT + m * h * 2 + m * n * 2, "flops": 2.0 * m * h * 2 * n}
 
