@@ -5,14 +5,18 @@ and prefill TFLOP/s as the roofline terms), one process per GPU.
 
 Workloads (seeded synthetic weights and activations; no dataset exists):
   cfg0  Llama-3.2-1B FFN layer (H 2048, I 8192), decode, M = 1
-  cfg1  the same layer, prefill, M in {128, 512, 2048}; default M = 2048        <- default
+  cfg1  the same layer, prefill, M in {128, 512, 2048}; default M = 2048
   cfg2  Llama-3.1-8B FFN stack, 32 layers (H 4096, I 14336), M in {1, 8, 32, 4096}
   cfg3  Qwen2.5-14B FFN stack, 48 layers (H 5120, I 13824), M in {1, 4096}
-  cfg4  Llama-3-70B FFN stack, 80 layers (H 8192, I 28672), M in {1, 4, 16, 64, 8192}
-A step is one pass of M tokens through the workload's layers (each layer gets its own fresh
-normalised input, as the activations between FFN layers pass through a norm). With N > 1 the
-layers are tensor-partitioned across the ranks (gate/up column-, down row-parallel, one NCCL
-all-reduce per layer): total work is fixed, "scaling": "strong".
+  cfg4  Llama-3-70B FFN stack, 80 layers (H 8192, I 28672), M in {1, 4, 16, 64, 8192};
+        default M = 8192                                                      <- default
+cfg4 is the default because BASELINE.json reports it at 1/2/4/8 GPUs and its scaling target names
+it; the single-layer cfg1 is the per-kernel case (--workload cfg1).
+A step is one pass of M tokens through the workload's layers, chained as a model chains them:
+h += FFN_l(RMSNorm(h)) per layer, the residual add and the next norm fused into one boundary
+launch. With N > 1 the layers are tensor-partitioned across the ranks (gate/up column-, down
+row-parallel) and the boundary also sums the rank partials over NVLink: total work is fixed,
+"scaling": "strong".
 
 Timing: W untimed warm-up steps, then K steps, each bracketed by CUDA events on the stream that
 runs it; a >L2 buffer is written between steps when the workload's weights fit in L2. Barrier +
@@ -35,7 +39,7 @@ CONFIGS = {
     "cfg1": dict(model="llama3.2-1b-ffn", hidden=2048, inter=8192, layers=1, ms=[128, 512, 2048], m=2048),
     "cfg2": dict(model="llama3.1-8b-ffn-stack", hidden=4096, inter=14336, layers=32, ms=[1, 8, 32, 4096], m=1),
     "cfg3": dict(model="qwen2.5-14b-ffn-stack", hidden=5120, inter=13824, layers=48, ms=[1, 4096], m=1),
-    "cfg4": dict(model="llama3-70b-ffn-stack", hidden=8192, inter=28672, layers=80, ms=[1, 4, 16, 64, 8192], m=1),
+    "cfg4": dict(model="llama3-70b-ffn-stack", hidden=8192, inter=28672, layers=80, ms=[1, 4, 16, 64, 8192], m=8192),
 }
 L2_BYTES = 126 * 2**20
 
@@ -69,7 +73,7 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="cfg1", choices=sorted(CONFIGS))
+    ap.add_argument("--workload", default="cfg4", choices=sorted(CONFIGS))
     ap.add_argument("--m", "--tokens", dest="m", type=int, default=0,
                     help="tokens per step (default: the workload's); --tokens under torchrun")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (testing only)")
@@ -206,8 +210,9 @@ def run_hmb(args):
     h, inter, L, m = wl["hidden"], wl["inter"], wl["layers"], wl["m"]
 
     # Weights: layer l drawn on the device from seed 1000 + l; with N > 1 each rank keeps its shard.
+    # RMSNorm weights 1 + 0.2 N(0, 1) (seed 2000 + l), as the reference's boundary test draws them.
     tp = TensorParallelFfn(h, inter, rank=rank, world=world) if world > 1 else None
-    layers = []
+    layers, norms = [], []
     gen = torch.Generator(device=dev)
     for l in range(L):
         gen.manual_seed(1000 + l)
@@ -219,29 +224,30 @@ def run_hmb(args):
         else:
             layers.append(H.slice_packed_ffn(g, u, d, h, inter, 0, inter, H.GateUpLayout.kInterleaved))
         del g, u, d
+        gen.manual_seed(2000 + l)
+        norms.append((torch.randn(h, device=dev, generator=gen) * 0.2 + 1.0).to(torch.bfloat16))
     torch.cuda.synchronize()
     if tp is not None:
         tp.connect(m, dev)  # the NVLink boundary-sum buffers, before any capture
     trace("weights ready")
-    stack = FfnStack(layers, h, dev, tp=tp)
-    n_local = stack.layers[0].channels()
+    stack = FfnStack(layers, h, dev, tp=tp, norms=norms)
 
-    # Activations: fresh N(0, 1) input per layer (seed 7), resident in HBM.
+    # The stack's input: the residual stream h_0 ~ N(0, 1) (seed 7), resident in HBM; each layer
+    # reads RMSNorm of the running residual.
     gen.manual_seed(7)
-    x_all = torch.randn(L, m, h, device=dev, generator=gen).to(torch.bfloat16)
+    h0 = torch.randn(m, h, device=dev, generator=gen).to(torch.bfloat16)
     weights_local = sum(w.gate_up.numel() + w.down.numel() for w in stack.layers)
     flush = L2Flush(dev) if weights_local < 2 * L2_BYTES else None
 
     use_graph = not args.no_graph
     if use_graph:
-        graph, gx, gy = stack.graph(m)
+        graph, g_in, g_out = stack.graph(m)
         trace("graph captured")
-        gx.copy_(x_all)
+        g_in.copy_(h0)
         step = graph.replay
     else:
-        y_all = torch.empty_like(x_all)
-        scratch = stack._scratch(m)
-        step = lambda: stack.forward(x_all, y_all, scratch)  # noqa: E731
+        result, bufs = torch.empty_like(h0), stack.buffers(m)
+        step = lambda: stack.forward(h0, result, bufs)  # noqa: E731
     stream = torch.cuda.current_stream(dev)
 
     def barrier():
@@ -278,11 +284,11 @@ def run_hmb(args):
     trace("timed steps done", step_ms)
     # Dominant kernel, timed alone: the fused gate/up + SiLU*up kernel of layer 0.
     w0 = stack.layers[0]
-    dom = dominant_kernel(stack, w0, x_all[0], flush, stream, m)
+    dom = dominant_kernel(stack, w0, h0, flush, stream, m)
 
     trace("dominant kernel done")
     # End to end through the public API with host buffers (H2D of the step's inputs, D2H of its outputs).
-    e2e = end_to_end(stack, x_all, m, args, flush, barrier, world, dev)
+    e2e = end_to_end(stack, h0, m, args, flush, barrier, world, dev)
     trace("e2e done")
 
     pk, pk_kind = peaks()
@@ -308,7 +314,7 @@ def run_hmb(args):
     line = {
         "metric": "ffn_tokens_per_s", "value": round(tokens_per_s, 2), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded W4A16 group-128, N(0,1) bf16)",
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded W4A16 group-128 weights, RMSNorm weights 1+0.2N(0,1), N(0,1) bf16 input)",
         "config": {"workload": f"{wl['name']}: {wl['model']} x{L} layers, M={m}", "hidden": h, "intermediate": inter,
                    "layers": L, "m": m, "parallelism": f"tp{world}" if world > 1 else "single",
                    "l2": "flushed between steps (2x L2 buffer written, then read)" if flush is not None else "weights larger than L2",
@@ -373,11 +379,11 @@ def dominant_kernel(stack, w, x, flush, stream, m, reps=20):
             "bytes": h * 2 * n * BYTES_PER_WEIGHT + m * h * 2 + m * n * 2, "flops": 2.0 * m * h * 2 * n}
 
 
-def end_to_end(stack, x_all, m, args, flush, barrier, world, dev):
+def end_to_end(stack, h0, m, args, flush, barrier, world, dev):
     import torch
     import torch.distributed as dist
 
-    x_host = x_all.cpu().pin_memory()
+    x_host = h0.cpu().pin_memory()
     y_host = torch.empty_like(x_host).pin_memory()
     stream = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):

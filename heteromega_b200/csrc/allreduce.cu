@@ -1,24 +1,32 @@
-// Tensor-parallel boundary sum over NVLink peer memory: y = sum over the P ranks of each rank's y,
-// in place, identical bits on every rank (fp32 sums in rank order, one rounding to the output type).
-// It replaces the per-layer NCCL all-reduce of the rank partials and the reference's boundary sum
-// residual_add2 / MergedFfn::add_out (kernels/gpu/src/residual_add.cu:55-73,
-// src/unified_llm_w4a16_hetero/merged_ffn.cpp:417).
+// Tensor-parallel boundary over NVLink peer memory, two kernels on one communicator:
+//   allreduce_kernel: y = the sum over the P ranks of each rank's y, in place, identical bits on
+//     every rank (fp32 sums in rank order, one rounding to the output type). It replaces the
+//     per-layer all-reduce of the rank partials and the reference's boundary sum residual_add2 /
+//     MergedFfn::add_out (kernels/gpu/src/residual_add.cu:55-73,
+//     src/unified_llm_w4a16_hetero/merged_ffn.cpp:417).
+//   boundary_kernel: the whole layer boundary in one launch: x += the rank partials, then RMSNorm
+//     of x into the next layer's input, which lands in every rank's output region. It replaces
+//     residual_norm_bf16 on the summed partials (kernels/gpu/src/residual_norm.cu:38-87,
+//     src/unified_llm_w4a16_hetero/unified_llm_w4a16.cpp:2533-2540).
 //
 // Every rank allocates one symmetric buffer (cudaMalloc) and opens its peers' through CUDA IPC
-// handles; the buffer holds receive slots and flag words. Plain stores and loads over NVLink only:
-// no multicast, no library kernel on peer memory.
+// handles; the buffer holds flag words, receive slots and the output region. Plain stores and loads
+// over NVLink only: no multicast, no library kernel on peer memory.
 //
 // The grid is always kCtas CTAs. Byte block i (4 KB) of a message or slot belongs to CTA i % kCtas
-// on every rank and in every call, whatever the message size, so a CTA only ever touches its own
-// blocks and synchronizes only with the same CTA of the other ranks, through flag words that carry
-// a per-CTA epoch (incremented at every call, the same on all ranks because every rank makes the
-// same calls). Receive slots are double-buffered by epoch parity: CTA b cannot be two calls ahead of
-// CTA b of a peer, because finishing a call needs every peer's contribution to it.
-//   one-shot (small messages): each rank stores its sub-range into every rank's slot[parity][me],
+// on every rank and in every call, whatever the message size, so a CTA only ever copies its own
+// blocks, and it synchronizes with the same CTA of the other ranks through flag words that carry a
+// per-CTA epoch (incremented at every call of either kernel, the same on all ranks because every
+// rank makes the same calls). Receive slots are double-buffered by epoch parity: a CTA cannot be
+// two calls ahead of the same CTA of a peer, because finishing a call needs every peer's
+// contribution to it.
+//   one-shot (small messages): each rank stores its message into every rank's slot[parity][me],
 //     raises its flag there, waits for every rank's flag, and sums the P slots in rank order.
 //   two-shot (large): the message is cut into P chunks; rank c owns chunk c. Reduce-scatter: each
 //     rank stores its part of chunk c into rank c's slot; rank c sums them in rank order. Gather: rank
 //     c stores the rounded sum into every rank's gather slot; each rank copies the chunks into y.
+// The boundary kernel cuts by rows instead (a row needs all its values for the norm): rank c owns
+// rows [c*m/P, (c+1)*m/P). Its CTAs process whole rows, so they wait for the flags of every CTA.
 // Every wait gives up after spin_limit_ns (default one second) and ORs 1 into the device status word.
 #include <cuda.h>
 
@@ -27,6 +35,8 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "norm_internal.h"
+#include "rownorm.cuh"
 
 namespace hmb {
 namespace {
@@ -37,22 +47,40 @@ constexpr int kThreads = 256;    // 16 bytes each: one 4 KB block per pass
 constexpr int64_t kBlock = 4096;
 constexpr size_t kFlagBytes = 2 * 2 * kMaxRanks * kCtas * 4;  // [phase][parity][rank][cta]
 constexpr int64_t kOneShotBytes = 512 * 1024;
+constexpr size_t kRowSlack = 2 * kRowMaxH;  // a row-cut chunk can exceed 1/P of a message by one row
+static_assert(kThreads == kRowThreads, "the boundary kernel processes rows with the whole CTA");
 
 struct Peers {
     uint8_t *base[kMaxRanks];  // every rank's symmetric buffer (this rank's included)
 };
 
-struct ArArgs {
+// What both kernels need to reach the peers and to synchronize with them.
+struct Link {
     Peers p;
-    void *y;
-    int64_t elems;
-    int dtype;  // HMB_BF16, HMB_FP16 or HMB_FP32
     int rank, world;
-    int two_shot;
     int64_t slot_bytes;  // bytes of one receive slot
     unsigned *epochs;    // this rank's per-CTA call counters (device memory)
     int *status;
     uint64_t limit_ns;
+};
+
+struct ArArgs {
+    Link l;
+    void *y;
+    int64_t elems;
+    int two_shot;
+};
+
+struct BnArgs {
+    Link l;
+    const uint16_t *y;  // this rank's partial [m, h]
+    uint16_t *x;        // the residual [m, h]
+    const uint16_t *w;  // norm weight [h], or null
+    int64_t m;
+    int h;
+    float eps;
+    int two_shot;
+    int64_t out_offset;  // of the output region in every symmetric buffer
 };
 
 __device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
@@ -70,25 +98,35 @@ __device__ __forceinline__ uint64_t now_ns() {
 }
 
 // Flag word (phase, parity, from-rank, cta) in the buffer of rank `owner`.
-__device__ __forceinline__ unsigned *flag(const ArArgs &a, int owner, int phase, int parity, int from, int cta) {
-    return reinterpret_cast<unsigned *>(a.p.base[owner]) + ((phase * 2 + parity) * kMaxRanks + from) * kCtas + cta;
+__device__ __forceinline__ unsigned *flag(const Link &l, int owner, int phase, int parity, int from, int cta) {
+    return reinterpret_cast<unsigned *>(l.p.base[owner]) + ((phase * 2 + parity) * kMaxRanks + from) * kCtas + cta;
 }
 // Receive slot (phase 0: reduce-scatter / one-shot, phase 1: gather) for data from rank `from`.
-__device__ __forceinline__ uint8_t *slot(const ArArgs &a, int owner, int phase, int parity, int from) {
-    return a.p.base[owner] + kFlagBytes + ((static_cast<int64_t>(phase) * 2 + parity) * a.world + from) * a.slot_bytes;
+__device__ __forceinline__ uint8_t *slot(const Link &l, int owner, int phase, int parity, int from) {
+    return l.p.base[owner] + kFlagBytes + ((static_cast<int64_t>(phase) * 2 + parity) * l.world + from) * l.slot_bytes;
 }
 
-// Threads of this CTA wait (thread 0 spins, bounded) until rank `from`'s flag reaches `epoch`.
-__device__ __forceinline__ bool wait_flag(const ArArgs &a, const unsigned *f, unsigned epoch) {
+// Spins (bounded) until the flag reaches `epoch`.
+__device__ __forceinline__ bool wait_flag(const Link &l, const unsigned *f, unsigned epoch) {
     const uint64_t start = now_ns();
     for (uint32_t i = 0;; ++i) {
         if (static_cast<int>(ld_acquire_sys(f) - epoch) >= 0) return true;
-        if ((i & 15) == 15 && now_ns() - start > a.limit_ns) {
-            atomicOr(a.status, 1);
+        if ((i & 15) == 15 && now_ns() - start > l.limit_ns) {
+            atomicOr(l.status, 1);
             return false;
         }
         __nanosleep(32);
     }
+}
+
+// This CTA's call number (the same on every rank); *ok = 1.
+__device__ __forceinline__ unsigned begin_call(const Link &l, unsigned *s_epoch, int *ok) {
+    if (threadIdx.x == 0) {
+        *s_epoch = ++l.epochs[blockIdx.x];
+        *ok = 1;
+    }
+    __syncthreads();
+    return *s_epoch;
 }
 
 template <typename T>
@@ -167,15 +205,30 @@ __device__ __forceinline__ void sum_blocks(int world, uint8_t *out, const uint8_
     }
 }
 
-// Raises this CTA's flag `phase` on every rank, then waits (bounded) for every rank's flag here.
-__device__ __forceinline__ bool exchange_flags(const ArArgs &a, int phase, int par, unsigned epoch, int *ok) {
+// Raises this CTA's flag `phase` on every rank (after the CTA's stores of the phase).
+__device__ __forceinline__ void raise_flags(const Link &l, int phase, int par, unsigned epoch) {
     __syncthreads();  // this CTA's stores of the phase are issued
-    if (threadIdx.x < a.world) {
-        // release at system scope after the CTA barrier: this CTA's stores (to peers too) are visible
-        // to whoever acquires the flag
-        st_release_sys(flag(a, threadIdx.x, phase, par, a.rank, blockIdx.x), epoch);
-        if (!wait_flag(a, flag(a, a.rank, phase, par, threadIdx.x, blockIdx.x), epoch)) *ok = 0;
-    }
+    // release at system scope after the CTA barrier: this CTA's stores (to peers too) are visible
+    // to whoever acquires the flag
+    if (threadIdx.x < l.world) st_release_sys(flag(l, threadIdx.x, phase, par, l.rank, blockIdx.x), epoch);
+}
+
+// Raises this CTA's flag `phase` on every rank, then waits (bounded) for every rank's flag of the
+// same CTA here.
+__device__ __forceinline__ bool exchange_flags(const Link &l, int phase, int par, unsigned epoch, int *ok) {
+    raise_flags(l, phase, par, epoch);
+    if (threadIdx.x < l.world && !wait_flag(l, flag(l, l.rank, phase, par, threadIdx.x, blockIdx.x), epoch)) *ok = 0;
+    __syncthreads();
+    return *ok != 0;
+}
+
+// Waits (bounded) until every CTA of every rank has raised its flag `phase` here.
+__device__ __forceinline__ bool wait_all_ctas(const Link &l, int phase, int par, unsigned epoch, int *ok) {
+    for (int i = threadIdx.x; i < l.world * kCtas; i += blockDim.x)
+        if (!wait_flag(l, flag(l, l.rank, phase, par, i / kCtas, i % kCtas), epoch)) {
+            *ok = 0;
+            break;
+        }
     __syncthreads();
     return *ok != 0;
 }
@@ -184,12 +237,8 @@ template <typename T>
 __global__ void __launch_bounds__(kThreads, 1) allreduce_kernel(const ArArgs a) {
     __shared__ unsigned s_epoch;
     __shared__ int s_ok;
-    if (threadIdx.x == 0) {
-        s_epoch = ++a.epochs[blockIdx.x];
-        s_ok = 1;
-    }
-    __syncthreads();
-    const unsigned epoch = s_epoch;
+    const Link &l = a.l;
+    const unsigned epoch = begin_call(l, &s_epoch, &s_ok);
     const int par = epoch & 1;
     uint8_t *y = static_cast<uint8_t *>(a.y);
     const int64_t bytes = a.elems * static_cast<int64_t>(sizeof(T));
@@ -197,30 +246,85 @@ __global__ void __launch_bounds__(kThreads, 1) allreduce_kernel(const ArArgs a) 
 
     if (!a.two_shot) {
         // One-shot: this rank's message into every rank's slot[me]; then sum the P slots here.
-        for (int r = 0; r < a.world; ++r) copy_blocks(slot(a, r, 0, par, a.rank), y, bytes);
-        if (!exchange_flags(a, 0, par, epoch, &s_ok)) return;
-        for (int r = 0; r < a.world; ++r) in[r] = slot(a, a.rank, 0, par, r);
-        sum_blocks<T>(a.world, y, in, bytes);
+        for (int r = 0; r < l.world; ++r) copy_blocks(slot(l, r, 0, par, l.rank), y, bytes);
+        if (!exchange_flags(l, 0, par, epoch, &s_ok)) return;
+        for (int r = 0; r < l.world; ++r) in[r] = slot(l, l.rank, 0, par, r);
+        sum_blocks<T>(l.world, y, in, bytes);
         return;
     }
 
     // Two-shot. Chunk c = bytes [c * chunk, (c + 1) * chunk) of the message; rank c owns it.
-    const int64_t chunk = ((bytes + a.world - 1) / a.world + 15) / 16 * 16;
+    const int64_t chunk = ((bytes + l.world - 1) / l.world + 15) / 16 * 16;
     auto chunk_bytes = [&](int c) { return std::max<int64_t>(0, std::min<int64_t>(chunk, bytes - c * chunk)); };
     // Reduce-scatter: chunk c of this rank's message into rank c's slot[me].
-    for (int c = 0; c < a.world; ++c) copy_blocks(slot(a, c, 0, par, a.rank), y + c * chunk, chunk_bytes(c));
-    if (!exchange_flags(a, 0, par, epoch, &s_ok)) return;
+    for (int c = 0; c < l.world; ++c) copy_blocks(slot(l, c, 0, par, l.rank), y + c * chunk, chunk_bytes(c));
+    if (!exchange_flags(l, 0, par, epoch, &s_ok)) return;
     // The sum of this rank's chunk, in rank order, into this rank's gather slot[me], then into every
     // other rank's gather slot[me].
-    uint8_t *mine = slot(a, a.rank, 1, par, a.rank);
-    for (int r = 0; r < a.world; ++r) in[r] = slot(a, a.rank, 0, par, r);
-    sum_blocks<T>(a.world, mine, in, chunk_bytes(a.rank));
+    uint8_t *mine = slot(l, l.rank, 1, par, l.rank);
+    for (int r = 0; r < l.world; ++r) in[r] = slot(l, l.rank, 0, par, r);
+    sum_blocks<T>(l.world, mine, in, chunk_bytes(l.rank));
     __syncthreads();
-    for (int r = 0; r < a.world; ++r)
-        if (r != a.rank) copy_blocks(slot(a, r, 1, par, a.rank), mine, chunk_bytes(a.rank));
-    if (!exchange_flags(a, 1, par, epoch, &s_ok)) return;
+    for (int r = 0; r < l.world; ++r)
+        if (r != l.rank) copy_blocks(slot(l, r, 1, par, l.rank), mine, chunk_bytes(l.rank));
+    if (!exchange_flags(l, 1, par, epoch, &s_ok)) return;
     // Gather: chunk c from gather slot[c] into y.
-    for (int c = 0; c < a.world; ++c) copy_blocks(y + c * chunk, slot(a, a.rank, 1, par, c), chunk_bytes(c));
+    for (int c = 0; c < l.world; ++c) copy_blocks(y + c * chunk, slot(l, l.rank, 1, par, c), chunk_bytes(c));
+}
+
+// First row of rank c's share of m rows.
+__host__ __device__ __forceinline__ int64_t share_row(int64_t m, int world, int c) { return m * c / world; }
+
+// The layer boundary. One-shot: every rank gets every partial and computes every row (the residual
+// stays whole on every rank). Two-shot: rank c receives the rows it owns from every rank, computes
+// them, keeps x for those rows, and stores the normed rows into every rank's output region.
+__global__ void __launch_bounds__(kThreads, 1) boundary_kernel(const BnArgs a) {
+    __shared__ unsigned s_epoch;
+    __shared__ int s_ok;
+    __shared__ float red[kRowThreads / 32];
+    const Link &l = a.l;
+    // The next kernel may start its prologue; it waits for this grid before it reads the output.
+    pdl_launch_dependents();
+    pdl_wait();  // y comes from the previous kernel
+    const unsigned epoch = begin_call(l, &s_epoch, &s_ok);
+    const int par = epoch & 1;
+    const int64_t row_bytes = 2 * static_cast<int64_t>(a.h);
+    const uint8_t *y = reinterpret_cast<const uint8_t *>(a.y);
+    const uint16_t *in[kMaxRanks];
+    uint16_t *out[kMaxRanks];
+
+    if (!a.two_shot) {
+        for (int r = 0; r < l.world; ++r)
+            if (r != l.rank) copy_blocks(slot(l, r, 0, par, l.rank), y, a.m * row_bytes);
+        raise_flags(l, 0, par, epoch);
+        if (!wait_all_ctas(l, 0, par, epoch, &s_ok)) return;
+        for (int64_t row = blockIdx.x; row < a.m; row += kCtas) {
+            for (int r = 0; r < l.world; ++r)
+                in[r] = r == l.rank ? a.y + row * a.h : reinterpret_cast<const uint16_t *>(slot(l, l.rank, 0, par, r) + row * row_bytes);
+            out[0] = reinterpret_cast<uint16_t *>(l.p.base[l.rank] + a.out_offset) + row * a.h;
+            boundary_row(in, l.world, a.x + row * a.h, true, a.w, a.h, a.eps, out, 1, red);
+        }
+        return;
+    }
+
+    // Reduce-scatter by rows: rank c's rows of this rank's partial into rank c's slot[me].
+    for (int c = 0; c < l.world; ++c) {
+        const int64_t r0 = share_row(a.m, l.world, c), r1 = share_row(a.m, l.world, c + 1);
+        if (c != l.rank) copy_blocks(slot(l, c, 0, par, l.rank), y + r0 * row_bytes, (r1 - r0) * row_bytes);
+    }
+    raise_flags(l, 0, par, epoch);
+    if (!wait_all_ctas(l, 0, par, epoch, &s_ok)) return;
+    const int64_t r0 = share_row(a.m, l.world, l.rank), r1 = share_row(a.m, l.world, l.rank + 1);
+    for (int64_t row = r0 + blockIdx.x; row < r1; row += kCtas) {
+        for (int r = 0; r < l.world; ++r) {
+            in[r] = r == l.rank ? a.y + row * a.h : reinterpret_cast<const uint16_t *>(slot(l, l.rank, 0, par, r) + (row - r0) * row_bytes);
+            out[r] = reinterpret_cast<uint16_t *>(l.p.base[r] + a.out_offset) + row * a.h;
+        }
+        boundary_row(in, l.world, a.x + row * a.h, true, a.w, a.h, a.eps, out, l.world, red);
+    }
+    // The kernel ends only when every rank's rows have arrived in this rank's output region.
+    raise_flags(l, 1, par, epoch);
+    wait_all_ctas(l, 1, par, epoch, &s_ok);
 }
 
 }  // namespace
@@ -232,11 +336,28 @@ struct hmb_comm {
     int rank = 0, world = 1, device = 0;
     size_t max_bytes = 0;   // largest message
     size_t slot_bytes = 0;  // one receive slot
+    size_t out_offset = 0;  // output region of the boundary, max_bytes long
     uint8_t *mine = nullptr;
     unsigned *epochs = nullptr;
     Peers peers{};
     bool connected = false;
 };
+
+namespace {
+
+Link make_link(const hmb_comm *c, uint64_t spin_limit_ns, int *status) {
+    Link l{};
+    l.p = c->peers;
+    l.rank = c->rank;
+    l.world = c->world;
+    l.slot_bytes = static_cast<int64_t>(c->slot_bytes);
+    l.epochs = c->epochs;
+    l.status = status;
+    l.limit_ns = spin_limit_ns ? spin_limit_ns : 1000000000ull;
+    return l;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -248,10 +369,12 @@ int hmb_comm_create(int rank, int world, size_t max_bytes, hmb_comm **out, void 
     c->rank = rank;
     c->world = world;
     cudaGetDevice(&c->device);
-    c->max_bytes = (max_bytes + 15) / 16 * 16;
-    // A one-shot slot holds a whole message (<= kOneShotBytes), a two-shot slot one chunk of it.
-    c->slot_bytes = std::max<size_t>(kOneShotBytes, ((c->max_bytes + world - 1) / world + 15) / 16 * 16);
-    const size_t bytes = kFlagBytes + 2 * 2 * static_cast<size_t>(world) * c->slot_bytes;
+    c->max_bytes = (max_bytes + 255) / 256 * 256;
+    // A one-shot slot holds a whole message (<= kOneShotBytes), a two-shot slot one chunk of it (for
+    // the boundary, one rank's rows: at most one row more than 1/P of the message).
+    c->slot_bytes = std::max<size_t>(kOneShotBytes, ((c->max_bytes + world - 1) / world + kRowSlack + 255) / 256 * 256);
+    c->out_offset = kFlagBytes + 2 * 2 * static_cast<size_t>(world) * c->slot_bytes;
+    const size_t bytes = c->out_offset + c->max_bytes;
     cudaError_t e = cudaMalloc(&c->mine, bytes);
     if (e == cudaSuccess) e = cudaMemset(c->mine, 0, kFlagBytes);
     if (e == cudaSuccess) e = cudaMalloc(&c->epochs, kCtas * sizeof(unsigned));
@@ -303,17 +426,10 @@ int hmb_allreduce_partials(void *y, int64_t elems, int dtype, hmb_comm *c, hmb_s
     int *status = device_status_word();
     if (!status) return HMB_ERR_CUDA;
     ArArgs a{};
-    a.p = c->peers;
+    a.l = make_link(c, spin_limit_ns, status);
     a.y = y;
     a.elems = elems;
-    a.dtype = dtype;
-    a.rank = c->rank;
-    a.world = c->world;
     a.two_shot = bytes > kOneShotBytes;
-    a.slot_bytes = static_cast<int64_t>(c->slot_bytes);
-    a.epochs = c->epochs;
-    a.status = status;
-    a.limit_ns = spin_limit_ns ? spin_limit_ns : 1000000000ull;
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (dtype == HMB_FP32)
         allreduce_kernel<float><<<kCtas, kThreads, 0, s>>>(a);
@@ -322,6 +438,57 @@ int hmb_allreduce_partials(void *y, int64_t elems, int dtype, hmb_comm *c, hmb_s
     else
         allreduce_kernel<__half><<<kCtas, kThreads, 0, s>>>(a);
     return launch_status();
+}
+
+int hmb_comm_out(hmb_comm *c, void **ptr, size_t *bytes) {
+    if (!c || !ptr) return HMB_ERR_ARG;
+    *ptr = c->mine + c->out_offset;
+    if (bytes) *bytes = c->max_bytes;
+    return HMB_OK;
+}
+
+int hmb_comm_rows(const hmb_comm *c, int64_t m, int64_t h, int64_t *begin, int64_t *end) {
+    if (!c || !begin || !end || m <= 0 || h <= 0) return HMB_ERR_ARG;
+    if (m * h * 2 <= kOneShotBytes || c->world == 1) {
+        *begin = 0;
+        *end = m;
+    } else {
+        *begin = share_row(m, c->world, c->rank);
+        *end = share_row(m, c->world, c->rank + 1);
+    }
+    return HMB_OK;
+}
+
+int hmb_allreduce_residual_norm(const void *y, void *x, const void *weight, int64_t m, int64_t h, float eps, hmb_comm *c,
+                                hmb_stream_t stream, uint64_t spin_limit_ns) {
+    if (!y || !x || !c || m <= 0 || h <= 0 || h % 8 || h > kRowMaxH || !(eps >= 0.0f)) return HMB_ERR_ARG;
+    if (!c->connected) return HMB_ERR_ARG;
+    if (!aligned(y, 16) || !aligned(x, 16) || (weight && !aligned(weight, 16))) return HMB_ERR_ALIGN;
+    const int64_t bytes = m * h * 2;
+    if (static_cast<size_t>(bytes) > c->max_bytes) return HMB_ERR_WORKSPACE;
+    void *out = c->mine + c->out_offset;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (c->world == 1) return residual_norm_launch(x, h, y, h, nullptr, 0, weight, out, h, m, h, eps, s);
+    const bool two_shot = bytes > kOneShotBytes;
+    if (two_shot && static_cast<size_t>((share_row(m, c->world, 1) + 1) * 2 * h) > c->slot_bytes) return HMB_ERR_WORKSPACE;
+    int *status = device_status_word();
+    if (!status) return HMB_ERR_CUDA;
+    BnArgs a{};
+    a.l = make_link(c, spin_limit_ns, status);
+    a.y = static_cast<const uint16_t *>(y);
+    a.x = static_cast<uint16_t *>(x);
+    a.w = static_cast<const uint16_t *>(weight);
+    a.m = m;
+    a.h = static_cast<int>(h);
+    a.eps = eps;
+    a.two_shot = two_shot;
+    a.out_offset = static_cast<int64_t>(c->out_offset);
+    const cudaError_t e = launch_pdl(boundary_kernel, dim3(kCtas), dim3(kThreads), 0, s, a);
+    if (e != cudaSuccess) {
+        set_cuda_error(e);
+        return HMB_ERR_CUDA;
+    }
+    return HMB_OK;
 }
 
 int hmb_comm_destroy(hmb_comm *c) {

@@ -1,0 +1,101 @@
+// One row of the layer boundary (residual add + RMSNorm), processed by one CTA of kRowThreads
+// threads. The single-GPU boundary (norm.cu) and the tensor-parallel one fused with the rank sum
+// (allreduce.cu) share it.
+//
+// The arithmetic is the reference's residual_norm_kernel (kernels/gpu/src/residual_norm.cu:38-87),
+// generalised from two addends to any number:
+//   x_new = bf16(((x + in_0) + in_1) + ...)    fp32, left to right, one rounding
+//   out   = bf16((x_new * rsqrt(sum(x_new^2) / h + eps)) * w)
+// The mean of squares is taken over the rounded values. Without w, out = x_new.
+#pragma once
+#include "common.cuh"
+
+namespace hmb {
+
+constexpr int kRowThreads = 256;
+constexpr int kRowMaxVec = 8;  // 16-byte vectors per thread: rows of up to 8 * 8 * 256 = 16384 values
+constexpr int kRowMaxH = kRowMaxVec * 8 * kRowThreads;
+
+// Sum of v over the CTA. Every thread gets the same bits: the warp totals are added in warp order.
+// red: kRowThreads / 32 floats of shared memory; all threads of the CTA must call.
+__device__ __forceinline__ float cta_sum(float v, float *red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kRowThreads / 32; ++i) t += red[i];
+    __syncthreads();
+    return t;
+}
+
+__device__ __forceinline__ void unpack8(const uint4 &v, float *f) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        f[2 * q] = bf16_to_f32(w[q] & 0xFFFFu);
+        f[2 * q + 1] = bf16hi_to_f32(w[q]);
+    }
+}
+
+__device__ __forceinline__ uint4 pack8(const float *f) {
+    uint32_t w[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) w[q] = f32_to_bf16(f[2 * q]) | (f32_to_bf16(f[2 * q + 1]) << 16);
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// in[0..n_in): addend rows (bf16, h values). x: the residual row, overwritten with x_new when
+// n_in > 0 and write_x. out[0..n_out): rows that all receive the result. w: the norm weight row or
+// null. h % 8 == 0, h <= kRowMaxH; every pointer 16-byte aligned. All threads of the CTA must call.
+__device__ __forceinline__ void boundary_row(const uint16_t *const *in, int n_in, uint16_t *x, bool write_x, const uint16_t *w,
+                                             int h, float eps, uint16_t *const *out, int n_out, float *red) {
+    const int nv = h >> 3;
+    uint4 xv[kRowMaxVec];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kRowMaxVec; ++i) {
+        const int v = i * kRowThreads + threadIdx.x;
+        if (v < nv) {
+            uint4 cur = *reinterpret_cast<const uint4 *>(x + 8 * v);
+            if (n_in > 0) {
+                float acc[8];
+                unpack8(cur, acc);
+                for (int r = 0; r < n_in; ++r) {
+                    float p[8];
+                    unpack8(*reinterpret_cast<const uint4 *>(in[r] + 8 * v), p);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc[e] += p[e];
+                }
+                cur = pack8(acc);
+                if (write_x) *reinterpret_cast<uint4 *>(x + 8 * v) = cur;
+            }
+            xv[i] = cur;
+            float f[8];
+            unpack8(cur, f);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
+        }
+    }
+    float scale = 1.0f;
+    if (w != nullptr) scale = rsqrtf(cta_sum(ss, red) / static_cast<float>(h) + eps);
+#pragma unroll
+    for (int i = 0; i < kRowMaxVec; ++i) {
+        const int v = i * kRowThreads + threadIdx.x;
+        if (v < nv) {
+            uint4 o = xv[i];
+            if (w != nullptr) {
+                float f[8], g[8];
+                unpack8(o, f);
+                unpack8(*reinterpret_cast<const uint4 *>(w + 8 * v), g);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) f[e] = f[e] * scale * g[e];
+                o = pack8(f);
+            }
+            for (int d = 0; d < n_out; ++d) *reinterpret_cast<uint4 *>(out[d] + 8 * v) = o;
+        }
+    }
+}
+
+}  // namespace hmb

@@ -55,10 +55,50 @@ class PeerComm:
               "hmb_allreduce_partials")
         return t
 
+    def out(self, m, h):
+        """bf16 [m, h] view of the output region of boundary() (valid while the communicator lives)."""
+        if m * h * 2 > self.max_bytes:
+            raise ValueError("PeerComm.out: larger than the communicator's max_bytes")
+        ptr, nbytes = ctypes.c_void_p(), ctypes.c_size_t()
+        check(lib().hmb_comm_out(self._ptr, ctypes.byref(ptr), ctypes.byref(nbytes)), "hmb_comm_out")
+        return torch.as_tensor(_DeviceArray(ptr.value, (m, h), self), device=self.device).view(torch.bfloat16)
+
+    def rows(self, m, h):
+        """[begin, end): the rows of an m x h boundary whose residual this rank keeps."""
+        b, e = ctypes.c_int64(), ctypes.c_int64()
+        check(lib().hmb_comm_rows(self._ptr, m, h, ctypes.byref(b), ctypes.byref(e)), "hmb_comm_rows")
+        return b.value, e.value
+
+    def boundary(self, y, x, weight=None, eps=1e-5, spin_limit_ns=0):
+        """The layer boundary (hmb_allreduce_residual_norm): x[rows] += the rank sum of y, then
+        RMSNorm(x) * weight (x itself without weight) into the output region, whose [m, h] view it
+        returns. y and x: contiguous bf16 [m, h] on this rank's GPU; weight bf16 [h] or None."""
+        m, h = x.shape
+        for name, t in (("y", y), ("x", x)):
+            if t.dtype != torch.bfloat16 or not t.is_contiguous() or tuple(t.shape) != (m, h) or t.device != self.device:
+                raise ValueError(f"PeerComm.boundary: {name} must be contiguous bf16 [m, h] on the communicator's device")
+        if weight is not None and (weight.dtype != torch.bfloat16 or weight.numel() != h or not weight.is_contiguous()):
+            raise ValueError("PeerComm.boundary: weight must be contiguous bf16 [h]")
+        out = self.out(m, h)
+        check(lib().hmb_allreduce_residual_norm(y.data_ptr(), x.data_ptr(), weight.data_ptr() if weight is not None else None,
+                                                m, h, float(eps), self._ptr, torch.cuda.current_stream(self.device).cuda_stream,
+                                                spin_limit_ns), "hmb_allreduce_residual_norm")
+        return out
+
     def close(self):
         if self._ptr is not None:
             check(lib().hmb_comm_destroy(self._ptr), "hmb_comm_destroy")
             self._ptr = None
+
+
+class _DeviceArray:
+    """A device buffer of int16 elements described by __cuda_array_interface__, so that torch can
+    view memory the library owns. Holds `owner` alive."""
+
+    def __init__(self, ptr, shape, owner):
+        self._owner = owner
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<i2", "data": (ptr, False), "version": 3,
+                                         "strides": None}
 
 
 class TensorParallelFfn:
@@ -129,6 +169,24 @@ class TensorParallelFfn:
             return self.comm.all_reduce(partial)
         dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group)
         return partial
+
+    def boundary(self, partial, h, weight, eps, normed=None):
+        """The layer boundary after this rank's partial of a layer: h += the sum of every rank's
+        partial, then the next input RMSNorm(h) * weight (h itself for weight None). Returns the
+        tensor that holds it: the communicator's output region (collective "hmb"; then only this
+        rank's rows of h are kept, see PeerComm.rows), else `normed` (NCCL all-reduce, then
+        hmb_residual_norm on every row). partial, h: bf16 [m, H] on this rank's GPU."""
+        if partial.is_cuda and self.world > 1 and self.collective == "hmb":
+            if self.comm is None:
+                raise RuntimeError("TensorParallelFfn: call connect(max_rows, device) on every rank first")
+            return self.comm.boundary(partial, h, weight, eps)
+        if self.world > 1:
+            dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group)
+        if weight is None:
+            ops.residual_norm(h, partial, None, None, None, eps)
+            return h
+        ops.residual_norm(h, partial, None, weight, normed, eps)
+        return normed
 
     def forward(self, layer, x, y):
         """y[m, H] (x's dtype) = the whole FFN layer for x, on every rank: this rank's partial written

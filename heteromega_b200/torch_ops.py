@@ -75,6 +75,7 @@ _defs.define("w4a16_ffn(Tensor(a!) y, Tensor x, Tensor gate_up, Tensor down, int
 _defs.define("w4a16_dequant(Tensor(a!) out, Tensor packed, int k, int n, int packed_k, int packed_n) -> ()")
 _defs.define("silu_mul(Tensor gate_up, Tensor(a!) act, int layout) -> ()")
 _defs.define("residual_add2(Tensor(a!) x, Tensor y_g, Tensor y_n) -> ()")
+_defs.define("residual_norm(Tensor(a!) x, Tensor? a, Tensor? b, Tensor? weight, Tensor(b!)? normed, float eps) -> ()")
 _defs.define("gather_tiles(Tensor(a!) dst, Tensor src0, Tensor src1, Tensor idx) -> ()")
 _defs.define("pack_w4a16_device(Tensor(a!) out, Tensor q, Tensor scales, Tensor zeros, Tensor(b!) bad) -> ()")
 
@@ -202,6 +203,25 @@ def _residual_add2(x, y_g, y_n):
                                   y_n.stride(0), _dtype_code(y_n), x.shape[0], x.shape[1], _stream(x)), "residual_add2")
 
 
+def _residual_norm(x, a, b, weight, normed, eps):
+    """x += a + b ((x + a) + b in fp32, one bf16 rounding), then normed = RMSNorm(x) * weight; the
+    arguments of heteromega::residual_norm_bf16 (kernels/gpu/include/heteromega/gpu_ffn.hpp:131-138)."""
+    _check_cuda(*[t for t in (x, a, b, weight, normed) if t is not None])
+    if x.dim() != 2 or x.dtype != torch.bfloat16 or x.stride(1) != 1:
+        raise ValueError("residual_norm: x must be bf16 [M, H] with a contiguous last dim")
+    if b is not None and a is None:
+        raise ValueError("residual_norm: b needs a")
+    for name, t in (("a", a), ("b", b), ("normed", normed)):
+        if t is not None and (t.dtype != torch.bfloat16 or t.dim() != 2 or tuple(t.shape) != tuple(x.shape) or t.stride(1) != 1):
+            raise ValueError(f"residual_norm: {name} must be bf16 shaped like x")
+    if weight is not None and (weight.dtype != torch.bfloat16 or weight.numel() != x.shape[1] or not weight.is_contiguous()):
+        raise ValueError("residual_norm: weight must be contiguous bf16 [H]")
+    check(lib().hmb_residual_norm(x.data_ptr(), x.stride(0), _ptr(a), a.stride(0) if a is not None else 0, _ptr(b),
+                                  b.stride(0) if b is not None else 0, _ptr(weight), _ptr(normed),
+                                  normed.stride(0) if normed is not None else 0, x.shape[0], x.shape[1], float(eps), _stream(x)),
+          "residual_norm")
+
+
 def _gather_tiles(dst, src0, src1, idx):
     _check_cuda(dst, src0, src1, idx)
     if idx.dtype != torch.int64 or not idx.is_contiguous():
@@ -226,6 +246,7 @@ _impls.impl("w4a16_ffn", _w4a16_ffn)
 _impls.impl("w4a16_dequant", _w4a16_dequant)
 _impls.impl("silu_mul", _silu_mul)
 _impls.impl("residual_add2", _residual_add2)
+_impls.impl("residual_norm", _residual_norm)
 _impls.impl("gather_tiles", _gather_tiles)
 _impls.impl("pack_w4a16_device", _pack_w4a16_device)
 

@@ -189,6 +189,29 @@ int hmb_comm_connect(hmb_comm *comm, const void *handles);
 int hmb_allreduce_partials(void *y, int64_t elems, int dtype, hmb_comm *comm, hmb_stream_t stream, uint64_t spin_limit_ns);
 int hmb_comm_destroy(hmb_comm *comm);
 
+/* The whole layer boundary of a tensor-parallel stack in one launch: the rank sum of hmb_allreduce_partials
+ * fused with residual_norm_bf16 (kernels/gpu/include/heteromega/gpu_ffn.hpp:131-138,
+ * kernels/gpu/src/residual_norm.cu:38-87; called between layers at
+ * src/unified_llm_w4a16_hetero/unified_llm_w4a16.cpp:2533-2540 with the GPU and NPU partials as its
+ * two addends). For every row owned by this rank:
+ *   x   = bf16(((x + y_0) + y_1) + ... + y_{P-1})            y_r = rank r's partial, fp32, one rounding
+ *   out = bf16((x * rsqrt(sum(x^2) / h + eps)) * weight)     weight null: out = x
+ * and `out`, the communicator's output region (hmb_comm_out), holds all m rows on every rank when the
+ * call completes, the same bits everywhere; it is the next layer's input. y, x: bf16 [m, h] rows, ld = h;
+ * weight bf16 [h]; h a multiple of 8, at most 16384; m * h * 2 at most the communicator's max_bytes
+ * (which must be the same on every rank). Messages up to 512 KB run one-shot: every rank owns every
+ * row, so x stays whole on every rank. Larger ones reduce-scatter by rows: rank c owns rows
+ * [c*m/P, (c+1)*m/P) (hmb_comm_rows), reads and updates only those rows of x, and stores its normed
+ * rows into every rank's output region; the other rows of x are neither read nor written. Every rank
+ * must make the same calls in the same order; waits give up after spin_limit_ns (0: one second) with
+ * HMB_ERR_TIMEOUT in the device status word. A group of one runs hmb_residual_norm into the output. */
+int hmb_allreduce_residual_norm(const void *y, void *x, const void *weight, int64_t m, int64_t h, float eps, hmb_comm *comm,
+                                hmb_stream_t stream, uint64_t spin_limit_ns);
+/* The output region of hmb_allreduce_residual_norm: *ptr (256-byte aligned), *bytes = max_bytes. */
+int hmb_comm_out(hmb_comm *comm, void **ptr, size_t *bytes);
+/* Rows [*begin, *end) of an m x h boundary whose residual this rank keeps (all rows when one-shot). */
+int hmb_comm_rows(const hmb_comm *comm, int64_t m, int64_t h, int64_t *begin, int64_t *end);
+
 /* Reads and clears the device status word of the current device: *status = HMB_ERR_TIMEOUT if a kernel
  * gave up a bounded wait since the last call, else HMB_OK. Synchronizes `stream`. */
 int hmb_device_status(int *status, hmb_stream_t stream);
@@ -197,6 +220,16 @@ int hmb_device_status(int *status, hmb_stream_t stream);
  * Replaces heteromega::silu_mul (gpu_ffn.hpp:92-93; silu_mul.cu:34-57). */
 int hmb_silu_mul(const void *gate_up, int64_t ld_in, void *act, int64_t ld_out, int64_t m, int64_t n, int layout,
                  hmb_stream_t stream);
+
+/* The layer boundary on one GPU: x[m, h] = bf16((x + a) + b) (fp32, one rounding; a and b may be null,
+ * b only with a; without a, x is not written), then normed = bf16((x * rsqrt(sum(x^2) / h + eps)) * weight)
+ * with the mean over the rounded x. weight null: no norm, normed (if not null) receives x. normed may be
+ * null. bf16 rows; h a multiple of 8, at most 16384; strides multiples of 8 elements; 16-byte aligned
+ * pointers. Replaces heteromega::residual_norm_bf16 (kernels/gpu/include/heteromega/gpu_ffn.hpp:131-138,
+ * kernels/gpu/src/residual_norm.cu:24-97) without its prepared-input side output: the GEMMs here read
+ * x in row order and form their own row sums. */
+int hmb_residual_norm(void *x, int64_t ldx, const void *a, int64_t lda, const void *b, int64_t ldb, const void *weight, void *normed,
+                      int64_t ldn, int64_t m, int64_t h, float eps, hmb_stream_t stream);
 
 /* x[m, cols] += y_g + y_n (partials first, fp32 math, one bf16 rounding); y_g, y_n bf16 or fp32.
  * Replaces heteromega::residual_add2 (gpu_ffn.hpp:159; residual_add.cu:55-73). */

@@ -59,6 +59,7 @@ def lib():
         L.orc_silu_mul.argtypes = [_ptr, _c_i64, _ptr, _c_i64, _c_i64, _c_i64, ctypes.c_int]
         L.orc_residual_add2.argtypes = [_ptr, _ptr, ctypes.c_int, _ptr, ctypes.c_int, _c_i64]
         L.orc_ffn.argtypes = [_ptr, _ptr, _c_i64, _c_i64, _c_i64, ctypes.c_int, _ptr, _c_i64, _ptr, _ptr, _ptr]
+        L.orc_residual_norm.argtypes = [_ptr, _ptr, ctypes.c_int, _ptr, _ptr, _c_i64, _c_i64, ctypes.c_float]
         _LIB = L
     return _LIB
 
@@ -146,6 +147,18 @@ def residual_add2(x_bits, y_g, y_n):
     yn = np.ascontiguousarray(y_n)
     lib().orc_residual_add2(_p(x), _p(yg), int(yg.dtype == np.float32), _p(yn), int(yn.dtype == np.float32), x.size)
     return x
+
+
+def residual_norm(x_bits, addends, weight_bits, eps, with_normed=True):
+    """The layer boundary (orc_residual_norm): addends is a list of bf16 bit arrays shaped like x (summed
+    into x in list order), weight_bits bf16 [h] or None. Returns (new x bits, normed bits or None)."""
+    x = np.ascontiguousarray(np.atleast_2d(x_bits), np.uint16).copy()
+    m, h = x.shape
+    add = np.ascontiguousarray(np.stack([np.atleast_2d(a) for a in addends]) if addends else np.zeros((0, m, h)), np.uint16)
+    w = None if weight_bits is None else np.ascontiguousarray(weight_bits, np.uint16)
+    normed = np.empty((m, h), np.uint16) if with_normed else None
+    lib().orc_residual_norm(_p(x), _p(add) if len(addends) else None, len(addends), _p(w), _p(normed), m, h, float(eps))
+    return x, normed
 
 
 def ffn(gate_up, down, h, n, stored, layout, x_bits):

@@ -199,6 +199,36 @@ void orc_residual_add2(uint16_t *x, const void *yg, int g32, const void *yn, int
     }
 }
 
+/* The layer boundary of residual_norm_kernel (kernels/gpu/src/residual_norm.cu:38-87) for any number
+ * of addends, as its test states the expected values (kernels/gpu/tests/test_gpu_ffn.cpp:266-268):
+ *   x      = bf16(((x + a_0) + a_1) + ...)              fp32, left to right, one rounding
+ *   normed = bf16((x * 1/sqrt(mean(x^2) + eps)) * w)    the mean over the rounded x
+ * addends: n_add bf16 arrays [m][h], one after the other; n_add 0 leaves x as it is. w null: normed = x.
+ * normed may be null. The sum of squares is taken in double here; a kernel's order differs, so its
+ * normed may differ from this by one bf16 unit in the last place. */
+void orc_residual_norm(uint16_t *x, const uint16_t *addends, int n_add, const uint16_t *w, uint16_t *normed, int64_t m, int64_t h,
+                       float eps) {
+    for (int64_t row = 0; row < m; ++row) {
+        uint16_t *xr = x + row * h;
+        double ss = 0.0;
+        for (int64_t c = 0; c < h; ++c) {
+            if (n_add > 0) {
+                float acc = orc_bf16_to_f32(xr[c]);
+                for (int r = 0; r < n_add; ++r) acc += orc_bf16_to_f32(addends[((int64_t)r * m + row) * h + c]);
+                xr[c] = orc_f32_to_bf16(acc);
+            }
+            const double v = orc_bf16_to_f32(xr[c]);
+            ss += v * v;
+        }
+        if (!normed) continue;
+        const float scale = (float)(1.0 / sqrt((double)(float)(ss / (double)h) + (double)eps));
+        for (int64_t c = 0; c < h; ++c) {
+            const float v = orc_bf16_to_f32(xr[c]);
+            normed[row * h + c] = w ? orc_f32_to_bf16(v * scale * orc_bf16_to_f32(w[c])) : xr[c];
+        }
+    }
+}
+
 /* One FFN channel slice as the model runs it on the reference CPU path
  * (unified_llm_w4a16.cpp:2873-2886 with the AVX GEMV): gate and up GEMVs with bf16 outputs,
  * fp32 SiLU*up rounded once, down GEMV. gate_up is packed [h, 2*stored] in `layout` order and

@@ -101,3 +101,30 @@ def test_oracle_against_reference_build(oracle):
     x = oracle.bf16_bits(rng.standard_normal(k))
     _, y16 = oracle.gemv(p, k, n, x[None])
     assert_bf16_close(y16[0], ref.gemv(x, p, k, n, threads=2), min_equal=0.98, what="oracle vs reference AVX")
+
+
+@pytest.mark.parametrize("addends", [2, 1, 0])
+def test_residual_norm_matches_reference_test_formula(oracle, addends):
+    """The oracle's layer boundary against the expected values of the reference's own boundary test,
+    evaluated in torch fp32 exactly as that test writes them (kernels/gpu/tests/test_gpu_ffn.cpp:262-268):
+    x = bf16(x + a + b), normed = x * rsqrt(mean(x^2) + eps) * weight. The same RMSNorm is the
+    reference model's CPU path (src/unified_llm_w4a16_hetero/unified_llm_w4a16.cpp:543-563)."""
+    import torch
+
+    g = torch.Generator().manual_seed(40 + addends)
+    m, h, eps = 96, 4096, 1e-5
+    rnd = lambda: torch.randn(m, h, generator=g).to(torch.bfloat16)  # noqa: E731
+    x, a, b = rnd(), rnd(), rnd()
+    weight = (torch.randn(h, generator=g) * 0.2 + 1.0).to(torch.bfloat16)
+    expected_x = x.float() + (a.float() if addends > 0 else 0) + (b.float() if addends > 1 else 0)
+    rounded_x = expected_x.to(torch.bfloat16).float()
+    expected = rounded_x * (rounded_x.square().mean(-1, keepdim=True) + eps).rsqrt() * weight.float()
+
+    bits = lambda t: t.view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+    got_x, got_n = oracle.residual_norm(bits(x), [bits(a), bits(b)][:addends], bits(weight), eps)
+    assert np.array_equal(got_x, bits(rounded_x.to(torch.bfloat16)))
+    assert_bf16_close(got_n, bits(expected.to(torch.bfloat16)), min_equal=0.999, what="oracle normed vs reference formula")
+    assert_close(oracle.bf16_to_f32(got_n), expected.numpy(), (1e-2, 5e-3, 0.99999), "EXACT tolerance of the reference test")
+    # without a weight the boundary only adds: normed carries x
+    x2, n2 = oracle.residual_norm(bits(x), [bits(a)], None, eps)
+    assert np.array_equal(x2, n2)

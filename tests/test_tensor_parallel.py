@@ -138,6 +138,30 @@ def _gpu_rank(rank, world, port, out_path, collective):
         other = mine.clone()
         dist.broadcast(other, src=0)
         res["same_bits"] = np.array(bool(torch.equal(mine, other)))
+
+        # The chained stack (h += FFN(RMSNorm(h)) per layer, boundary fused with the rank sum) against
+        # the single-GPU stack with the whole layers.
+        from heteromega_b200.stack import FfnStack
+
+        norms = [(torch.randn(hidden, device=dev, generator=gen) * 0.2 + 1.0).to(torch.bfloat16) for _ in range(2)]
+        tp.add_layer(g, u, d)  # a second layer (the same weights)
+        st_tp = FfnStack(None, hidden, dev, tp=tp, norms=norms)
+        st_one = FfnStack([full, full], hidden, dev, norms=norms)
+        same = []
+        for m in (1, 300):
+            gen.manual_seed(40 + m)
+            h0 = torch.randn(m, hidden, device=dev, generator=gen).to(torch.bfloat16)
+            got, ref = torch.empty_like(h0), torch.empty_like(h0)
+            st_tp.forward(h0, got)
+            graph, h_in, result = st_tp.graph(m)
+            h_in.copy_(h0)
+            graph.replay()
+            st_one.forward(h0, ref)
+            torch.cuda.synchronize()
+            same.append(bool(torch.equal(result, got)))
+            res[f"stack{m}"], res[f"stackref{m}"] = got.float().cpu().numpy(), ref.float().cpu().numpy()
+        res["stack_graph_same"] = np.array(all(same))
+        st_tp.release()
         from heteromega_b200.torch_ops import device_status
 
         res["status"] = np.array(device_status(dev))
@@ -148,6 +172,83 @@ def _gpu_rank(rank, world, port, out_path, collective):
             tp.close()
         dist.barrier(device_ids=[rank])
         dist.destroy_process_group()
+
+
+BOUNDARY_CASES = [(1, 2048), (7, 2048), (300, 2048), (1024, 2048), (32, 8192), (33, 8192)]
+
+
+def _gpu_boundary_rank(rank, world, port, out_path):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    comm = None
+    try:
+        from heteromega_b200.tensor_parallel import PeerComm
+
+        comm = PeerComm(1024 * 8192 * 2, device=dev)
+        res = {}
+        for rnd in range(2):  # the second round reuses the double-buffered slots with advanced epochs
+            for m, h in BOUNDARY_CASES:
+                for weighted in (True, False):
+                    tag = f"{m}_{h}_{int(weighted)}_{rnd}"
+                    gx = torch.Generator(device=dev).manual_seed(m * 31 + h + rnd)  # the same on every rank
+                    x = torch.randn(m, h, device=dev, generator=gx).to(torch.bfloat16)
+                    w = (torch.randn(h, device=dev, generator=gx) * 0.2 + 1.0).to(torch.bfloat16)
+                    gy = torch.Generator(device=dev).manual_seed(m * 31 + h + rnd + 1000 * (rank + 1))
+                    y = (torch.randn(m, h, device=dev, generator=gy) * 3).to(torch.bfloat16)
+                    x0 = x.clone()
+                    out = comm.boundary(y, x, w if weighted else None, 1e-5)
+                    torch.cuda.synchronize()
+                    b, e = comm.rows(m, h)
+                    bits = lambda t: t.cpu().view(torch.int16).numpy()  # noqa: E731
+                    res[f"x0_{tag}"], res[f"y_{tag}"], res[f"w_{tag}"] = bits(x0), bits(y), bits(w)
+                    res[f"out_{tag}"], res[f"x_{tag}"] = bits(out), bits(x[b:e])
+                    res[f"rows_{tag}"] = np.array([b, e])
+        from heteromega_b200.torch_ops import device_status
+
+        res["status"] = np.array(device_status(dev))
+        np.savez(out_path + f".{rank}.npz", **res)
+        dist.barrier(device_ids=[rank])
+    finally:
+        if comm is not None:
+            comm.close()
+        dist.barrier(device_ids=[rank])
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_two_gpu_boundary_matches_oracle(tmp_path, oracle):
+    """The fused tensor-parallel boundary (hmb_allreduce_residual_norm) on 2 GPUs, one-shot (up to 512 KB)
+    and two-shot (rows split between the ranks) sizes, with and without a norm weight, against the
+    oracle's boundary with the two rank partials as its addends in rank order: the kept rows of x bit
+    for bit, the output on both ranks the same bits and within one bf16 rounding of the oracle."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    out = str(tmp_path / "bn")
+    mp.start_processes(_gpu_boundary_rank, args=(2, free_port(), out), nprocs=2, join=True, start_method="spawn")
+    from metrics import assert_bf16_close
+
+    r = [np.load(out + f".{rank}.npz") for rank in range(2)]
+    assert int(r[0]["status"]) == 0 and int(r[1]["status"]) == 0
+    u16 = lambda a: a.view(np.uint16)  # noqa: E731
+    for rnd in range(2):
+        for m, h in BOUNDARY_CASES:
+            for weighted in (1, 0):
+                tag = f"{m}_{h}_{weighted}_{rnd}"
+                assert np.array_equal(r[0][f"out_{tag}"], r[1][f"out_{tag}"]), f"ranks disagree {tag}"
+                ref_x, ref_n = oracle.residual_norm(u16(r[0][f"x0_{tag}"]), [u16(r[0][f"y_{tag}"]), u16(r[1][f"y_{tag}"])],
+                                                    u16(r[0][f"w_{tag}"]) if weighted else None, 1e-5)
+                covered = np.zeros(m, bool)
+                for rank in range(2):
+                    b, e = r[rank][f"rows_{tag}"]
+                    covered[b:e] = True
+                    assert np.array_equal(u16(r[rank][f"x_{tag}"]), ref_x[b:e]), f"x rows {b}:{e} rank {rank} {tag}"
+                assert covered.all()
+                if weighted:
+                    assert_bf16_close(u16(r[0][f"out_{tag}"]), ref_n, min_equal=0.99, what=f"boundary out {tag}")
+                else:
+                    assert np.array_equal(u16(r[0][f"out_{tag}"]), ref_x), f"out without weight is x {tag}"
 
 
 @pytest.mark.gpu
@@ -167,3 +268,6 @@ def test_two_gpus(tmp_path, collective):
         assert bool(r["same_bits"])
         for m in (1, 7, 300, 1024):
             assert_close(r[f"got{m}"], r[f"ref{m}"], LEVEL, f"TP2 {collective} vs single GPU m={m} rank {rank}")
+        assert bool(r["stack_graph_same"])
+        for m in (1, 300):
+            assert_close(r[f"stack{m}"], r[f"stackref{m}"], LEVEL, f"TP2 {collective} chained stack m={m} rank {rank}")
