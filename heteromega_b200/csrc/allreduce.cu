@@ -34,6 +34,7 @@
 #include <cstring>
 #include <mutex>
 
+#include "comm_internal.h"
 #include "common.cuh"
 #include "norm_internal.h"
 #include "rownorm.cuh"
@@ -42,13 +43,14 @@ namespace hmb {
 namespace {
 
 constexpr int kMaxRanks = 8;
-constexpr int kCtas = 64;
+constexpr int kCtas = 128;
 constexpr int kThreads = 256;    // 16 bytes each: one 4 KB block per pass
 constexpr int64_t kBlock = 4096;
 constexpr size_t kFlagBytes = 2 * 2 * kMaxRanks * kCtas * 4;  // [phase][parity][rank][cta]
 constexpr int64_t kOneShotBytes = 512 * 1024;
 constexpr size_t kRowSlack = 2 * kRowMaxH;  // a row-cut chunk can exceed 1/P of a message by one row
 static_assert(kThreads == kRowThreads, "the boundary kernel processes rows with the whole CTA");
+static_assert(kMaxRanks == kCommMaxRanks, "one rank limit");
 
 struct Peers {
     uint8_t *base[kMaxRanks];  // every rank's symmetric buffer (this rank's included)
@@ -80,6 +82,7 @@ struct BnArgs {
     int h;
     float eps;
     int two_shot;
+    int prefilled;       // the partials are already in the slots (a scatter wrote them); y unused
     int64_t out_offset;  // of the output region in every symmetric buffer
 };
 
@@ -272,12 +275,10 @@ __global__ void __launch_bounds__(kThreads, 1) allreduce_kernel(const ArArgs a) 
     for (int c = 0; c < l.world; ++c) copy_blocks(y + c * chunk, slot(l, l.rank, 1, par, c), chunk_bytes(c));
 }
 
-// First row of rank c's share of m rows.
-__host__ __device__ __forceinline__ int64_t share_row(int64_t m, int world, int c) { return m * c / world; }
-
 // The layer boundary. One-shot: every rank gets every partial and computes every row (the residual
 // stays whole on every rank). Two-shot: rank c receives the rows it owns from every rank, computes
 // them, keeps x for those rows, and stores the normed rows into every rank's output region.
+template <int V, int NW>
 __global__ void __launch_bounds__(kThreads, 1) boundary_kernel(const BnArgs a) {
     __shared__ unsigned s_epoch;
     __shared__ int s_ok;
@@ -293,38 +294,68 @@ __global__ void __launch_bounds__(kThreads, 1) boundary_kernel(const BnArgs a) {
     const uint16_t *in[kMaxRanks];
     uint16_t *out[kMaxRanks];
 
+    // This rank's own partial: y, or (prefilled) its own slot like every other rank's.
+    const bool own_y = !a.prefilled;
     if (!a.two_shot) {
-        for (int r = 0; r < l.world; ++r)
-            if (r != l.rank) copy_blocks(slot(l, r, 0, par, l.rank), y, a.m * row_bytes);
+        if (!a.prefilled)
+            for (int r = 0; r < l.world; ++r)
+                if (r != l.rank) copy_blocks(slot(l, r, 0, par, l.rank), y, a.m * row_bytes);
         raise_flags(l, 0, par, epoch);
         if (!wait_all_ctas(l, 0, par, epoch, &s_ok)) return;
         for (int64_t row = blockIdx.x; row < a.m; row += kCtas) {
-            for (int r = 0; r < l.world; ++r)
-                in[r] = r == l.rank ? a.y + row * a.h : reinterpret_cast<const uint16_t *>(slot(l, l.rank, 0, par, r) + row * row_bytes);
+#pragma unroll
+            for (int r = 0; r < NW; ++r)
+                in[r] = r == l.rank && own_y ? a.y + row * a.h
+                                             : reinterpret_cast<const uint16_t *>(slot(l, l.rank, 0, par, r) + row * row_bytes);
             out[0] = reinterpret_cast<uint16_t *>(l.p.base[l.rank] + a.out_offset) + row * a.h;
-            boundary_row(in, l.world, a.x + row * a.h, true, a.w, a.h, a.eps, out, 1, red);
+            boundary_row<V, NW>(in, a.x + row * a.h, true, a.w, a.h, a.eps, out, 1, red);
         }
         return;
     }
 
     // Reduce-scatter by rows: rank c's rows of this rank's partial into rank c's slot[me].
-    for (int c = 0; c < l.world; ++c) {
-        const int64_t r0 = share_row(a.m, l.world, c), r1 = share_row(a.m, l.world, c + 1);
-        if (c != l.rank) copy_blocks(slot(l, c, 0, par, l.rank), y + r0 * row_bytes, (r1 - r0) * row_bytes);
-    }
+    if (!a.prefilled)
+        for (int c = 0; c < l.world; ++c) {
+            const int64_t r0 = comm_share_row(a.m, l.world, c), r1 = comm_share_row(a.m, l.world, c + 1);
+            if (c != l.rank) copy_blocks(slot(l, c, 0, par, l.rank), y + r0 * row_bytes, (r1 - r0) * row_bytes);
+        }
     raise_flags(l, 0, par, epoch);
     if (!wait_all_ctas(l, 0, par, epoch, &s_ok)) return;
-    const int64_t r0 = share_row(a.m, l.world, l.rank), r1 = share_row(a.m, l.world, l.rank + 1);
+    const int64_t r0 = comm_share_row(a.m, l.world, l.rank), r1 = comm_share_row(a.m, l.world, l.rank + 1);
     for (int64_t row = r0 + blockIdx.x; row < r1; row += kCtas) {
-        for (int r = 0; r < l.world; ++r) {
-            in[r] = r == l.rank ? a.y + row * a.h : reinterpret_cast<const uint16_t *>(slot(l, l.rank, 0, par, r) + (row - r0) * row_bytes);
+#pragma unroll
+        for (int r = 0; r < NW; ++r) {
+            in[r] = r == l.rank && own_y ? a.y + row * a.h
+                                         : reinterpret_cast<const uint16_t *>(slot(l, l.rank, 0, par, r) + (row - r0) * row_bytes);
             out[r] = reinterpret_cast<uint16_t *>(l.p.base[r] + a.out_offset) + row * a.h;
         }
-        boundary_row(in, l.world, a.x + row * a.h, true, a.w, a.h, a.eps, out, l.world, red);
+        boundary_row<V, NW>(in, a.x + row * a.h, true, a.w, a.h, a.eps, out, NW, red);
     }
     // The kernel ends only when every rank's rows have arrived in this rank's output region.
     raise_flags(l, 1, par, epoch);
     wait_all_ctas(l, 1, par, epoch, &s_ok);
+}
+
+template <int V>
+cudaError_t launch_boundary_v(int world, cudaStream_t s, const BnArgs &a) {
+    const dim3 g(kCtas), b(kThreads);
+    switch (world) {
+        case 1: return launch_pdl(boundary_kernel<V, 1>, g, b, 0, s, a);
+        case 2: return launch_pdl(boundary_kernel<V, 2>, g, b, 0, s, a);
+        case 3: return launch_pdl(boundary_kernel<V, 3>, g, b, 0, s, a);
+        case 4: return launch_pdl(boundary_kernel<V, 4>, g, b, 0, s, a);
+        case 5: return launch_pdl(boundary_kernel<V, 5>, g, b, 0, s, a);
+        case 6: return launch_pdl(boundary_kernel<V, 6>, g, b, 0, s, a);
+        case 7: return launch_pdl(boundary_kernel<V, 7>, g, b, 0, s, a);
+        default: return launch_pdl(boundary_kernel<V, 8>, g, b, 0, s, a);
+    }
+}
+
+cudaError_t launch_boundary(int v, int world, cudaStream_t s, const BnArgs &a) {
+    if (v == 1) return launch_boundary_v<1>(world, s, a);
+    if (v == 2) return launch_boundary_v<2>(world, s, a);
+    if (v == 4) return launch_boundary_v<4>(world, s, a);
+    return launch_boundary_v<8>(world, s, a);
 }
 
 }  // namespace
@@ -358,6 +389,62 @@ Link make_link(const hmb_comm *c, uint64_t spin_limit_ns, int *status) {
 }
 
 }  // namespace
+
+namespace hmb {
+
+int comm_scatter_target(const hmb_comm *c, int64_t m, int64_t h, ScatterTarget *t) {
+    if (!c || !t || m <= 0 || h <= 0 || h % 8) return HMB_ERR_ARG;
+    if (!c->connected) return HMB_ERR_ARG;
+    const int64_t bytes = m * h * 2;
+    if (static_cast<size_t>(bytes) > c->max_bytes) return HMB_ERR_WORKSPACE;
+    const bool all = bytes <= kOneShotBytes || c->world == 1;
+    if (!all && static_cast<size_t>((comm_share_row(m, c->world, 1) + 1) * 2 * h) > c->slot_bytes) return HMB_ERR_WORKSPACE;
+    *t = ScatterTarget{};
+    for (int r = 0; r < c->world; ++r) t->base[r] = c->peers.base[r];
+    t->slot0 = static_cast<int64_t>(kFlagBytes);
+    t->slot_bytes = static_cast<int64_t>(c->slot_bytes);
+    t->world = c->world;
+    t->rank = c->rank;
+    t->all = all;
+    t->m = m;
+    t->h = h;
+    t->epochs = c->epochs;
+    return HMB_OK;
+}
+
+int comm_boundary(hmb_comm *c, const void *y, void *x, const void *weight, int64_t m, int64_t h, float eps, bool prefilled,
+                  cudaStream_t s, uint64_t spin_limit_ns) {
+    if (!x || !c || m <= 0 || h <= 0 || h % 8 || h > kRowMaxH || !(eps >= 0.0f)) return HMB_ERR_ARG;
+    if (!c->connected || (!y && !prefilled)) return HMB_ERR_ARG;
+    if ((y && !aligned(y, 16)) || !aligned(x, 16) || (weight && !aligned(weight, 16))) return HMB_ERR_ALIGN;
+    const int64_t bytes = m * h * 2;
+    if (static_cast<size_t>(bytes) > c->max_bytes) return HMB_ERR_WORKSPACE;
+    void *out = c->mine + c->out_offset;
+    const bool two_shot = bytes > kOneShotBytes && c->world > 1;
+    if (two_shot && static_cast<size_t>((comm_share_row(m, c->world, 1) + 1) * 2 * h) > c->slot_bytes) return HMB_ERR_WORKSPACE;
+    if (c->world == 1 && !prefilled) return residual_norm_launch(x, h, y, h, nullptr, 0, weight, out, h, m, h, eps, s);
+    int *status = device_status_word();
+    if (!status) return HMB_ERR_CUDA;
+    BnArgs a{};
+    a.l = make_link(c, spin_limit_ns, status);
+    a.y = static_cast<const uint16_t *>(y);
+    a.x = static_cast<uint16_t *>(x);
+    a.w = static_cast<const uint16_t *>(weight);
+    a.m = m;
+    a.h = static_cast<int>(h);
+    a.eps = eps;
+    a.two_shot = two_shot;
+    a.prefilled = prefilled;
+    a.out_offset = static_cast<int64_t>(c->out_offset);
+    const cudaError_t e = launch_boundary(row_vectors(h), c->world, s, a);
+    if (e != cudaSuccess) {
+        set_cuda_error(e);
+        return HMB_ERR_CUDA;
+    }
+    return HMB_OK;
+}
+
+}  // namespace hmb
 
 extern "C" {
 
@@ -453,42 +540,16 @@ int hmb_comm_rows(const hmb_comm *c, int64_t m, int64_t h, int64_t *begin, int64
         *begin = 0;
         *end = m;
     } else {
-        *begin = share_row(m, c->world, c->rank);
-        *end = share_row(m, c->world, c->rank + 1);
+        *begin = comm_share_row(m, c->world, c->rank);
+        *end = comm_share_row(m, c->world, c->rank + 1);
     }
     return HMB_OK;
 }
 
 int hmb_allreduce_residual_norm(const void *y, void *x, const void *weight, int64_t m, int64_t h, float eps, hmb_comm *c,
                                 hmb_stream_t stream, uint64_t spin_limit_ns) {
-    if (!y || !x || !c || m <= 0 || h <= 0 || h % 8 || h > kRowMaxH || !(eps >= 0.0f)) return HMB_ERR_ARG;
-    if (!c->connected) return HMB_ERR_ARG;
-    if (!aligned(y, 16) || !aligned(x, 16) || (weight && !aligned(weight, 16))) return HMB_ERR_ALIGN;
-    const int64_t bytes = m * h * 2;
-    if (static_cast<size_t>(bytes) > c->max_bytes) return HMB_ERR_WORKSPACE;
-    void *out = c->mine + c->out_offset;
-    const cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (c->world == 1) return residual_norm_launch(x, h, y, h, nullptr, 0, weight, out, h, m, h, eps, s);
-    const bool two_shot = bytes > kOneShotBytes;
-    if (two_shot && static_cast<size_t>((share_row(m, c->world, 1) + 1) * 2 * h) > c->slot_bytes) return HMB_ERR_WORKSPACE;
-    int *status = device_status_word();
-    if (!status) return HMB_ERR_CUDA;
-    BnArgs a{};
-    a.l = make_link(c, spin_limit_ns, status);
-    a.y = static_cast<const uint16_t *>(y);
-    a.x = static_cast<uint16_t *>(x);
-    a.w = static_cast<const uint16_t *>(weight);
-    a.m = m;
-    a.h = static_cast<int>(h);
-    a.eps = eps;
-    a.two_shot = two_shot;
-    a.out_offset = static_cast<int64_t>(c->out_offset);
-    const cudaError_t e = launch_pdl(boundary_kernel, dim3(kCtas), dim3(kThreads), 0, s, a);
-    if (e != cudaSuccess) {
-        set_cuda_error(e);
-        return HMB_ERR_CUDA;
-    }
-    return HMB_OK;
+    if (!y) return HMB_ERR_ARG;
+    return comm_boundary(c, y, x, weight, m, h, eps, false, static_cast<cudaStream_t>(stream), spin_limit_ns);
 }
 
 int hmb_comm_destroy(hmb_comm *c) {

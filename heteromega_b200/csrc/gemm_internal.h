@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "comm_internal.h"
+
 namespace hmb {
 
 struct PairArgs {
@@ -27,6 +29,8 @@ struct PairArgs {
     int k_per_split; // K steps (of 64) per split
     float *split_ws;      // k_splits > 1: [tile][split][CTA] 128 x 256 fp32 sums
     unsigned *split_cnt;  // k_splits > 1: [tile][CTA] arrival and completion counters (self-resetting)
+    int scatter;          // HMB_EPI_STORE, 16-bit output: rows go to the communicator's receive slots `sc`
+    ScatterTarget sc;
 };
 
 // CTA pairs the pair kernel keeps resident on the current device.
@@ -38,10 +42,12 @@ size_t pair_split_bytes(int64_t m, int64_t k, int64_t n);
 
 // hmb_w4a16_gemm with an optional split-K workspace: split_ws (pair_split_bytes(m, k, n) bytes of
 // fp32 sums) and split_cnt (4 KB of counters, zero before the first call; the kernel leaves them
-// zero). Without them (nullptr) no K splits are used.
+// zero). Without them (nullptr) no K splits are used. With a scatter target (HMB_EPI_STORE, 16-bit
+// output, n == sc->h, m == sc->m) the output rows go to a communicator's receive slots instead of y,
+// always through the CTA-pair kernel.
 int gemm_run(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const void *x, int64_t ldx, int x_dtype, void *y, int64_t ldy,
              int y_dtype, int64_t m, int64_t k, int64_t n, int64_t start_col, int epilogue, int layout, void *split_ws, size_t split_ws_bytes,
-             unsigned *split_cnt, cudaStream_t stream);
+             unsigned *split_cnt, cudaStream_t stream, const ScatterTarget *sc = nullptr);
 constexpr size_t kSplitCounterBytes = 4096;
 
 // Launches the CTA-pair kernel; `map` is x as a 2D tensor map with 64 x 128 boxes (SWIZZLE_128B).

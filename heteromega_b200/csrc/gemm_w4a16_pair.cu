@@ -69,13 +69,24 @@ constexpr int kTmemCols = 256 * kAccStages;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory plan");
 static_assert(kBOff % 1024 == 0 && kPOff % 1024 == 0, "stage alignment");
 
+// 8 outputs (16 bytes) at column col of output row tok: into y, or over NVLink into the receive slots
+// of a tensor-parallel communicator (every rank's, or the row owner's).
+__device__ __forceinline__ void store_out16(const PairArgs &a, int par, int64_t tok, int64_t col, uint4 v) {
+    if (!a.scatter) {
+        *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.y) + tok * a.ldy + col) = v;
+        return;
+    }
+    const int nd = scatter_count(a.sc);
+    for (int d = 0; d < nd; ++d) *reinterpret_cast<uint4 *>(scatter_row(a.sc, par, tok, d) + col) = v;
+}
+
 // Epilogue of one split of a split-K tile, run by the 4 epilogue warps of a CTA (thread = row
 // 32 q + lane of this CTA's 128 rows). The split's fp32 sums go to its slot of the workspace and the
 // accumulator is released; the splits of the tile meet at a counter (all of them are resident); then
 // each split adds the slots, in split order, for its share of the rows and writes the outputs.
 template <bool F16, int EPI>
 __device__ __forceinline__ void split_epilogue(const PairArgs &a, uint32_t taddr, int unit, int tile, int mb, int nb, int rank,
-                                               int q, int lane, volatile int *abort, uint32_t release_bar) {
+                                               int q, int lane, volatile int *abort, uint32_t release_bar, int par) {
     const int S = a.k_splits, ks = unit % S, row = 32 * q + lane;
     constexpr int kRowFloats = 256, kSlotFloats = 128 * kRowFloats;
     float *part = a.split_ws + (static_cast<int64_t>(tile * S + ks) * 2 + rank) * kSlotFloats;
@@ -172,8 +183,7 @@ __device__ __forceinline__ void split_epilogue(const PairArgs &a, uint32_t taddr
                     uint32_t o[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) o[e] = to16<F16>(acc8[2 * e]) | (to16<F16>(acc8[2 * e + 1]) << 16);
-                    uint16_t *y = static_cast<uint16_t *>(a.y) + static_cast<int64_t>(tk) * a.ldy + nb * 256 + 8 * c8;
-                    *reinterpret_cast<uint4 *>(y) = make_uint4(o[0], o[1], o[2], o[3]);
+                    store_out16(a, par, tk, nb * 256 + 8 * c8, make_uint4(o[0], o[1], o[2], o[3]));
                 }
             }
         }
@@ -188,7 +198,7 @@ __device__ __forceinline__ void split_epilogue(const PairArgs &a, uint32_t taddr
 
 template <bool F16, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const PairArgs a) {
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ PairArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = smem_u32(smem);
@@ -402,6 +412,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Epilogue: warp q = warp % 4 reads TMEM lanes 32 q .. 32 q + 31 (rows of this CTA).
         const int q = warp & 3;
         pdl_wait();
+        // With a scatter target: the parity of the boundary call that will read the slots (the
+        // communicator's earlier calls have completed once pdl_wait returns).
+        const int par = a.scatter ? scatter_parity(a.sc) : 0;
         int t = 0;
         for (int unit = cluster; unit < num_units; unit += nclusters, ++t) {
             const int acc = t % kAccStages;
@@ -413,7 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t taddr = tmem + 256 * acc + (static_cast<uint32_t>(32 * q) << 16);
             if (a.k_splits > 1) {
                 split_epilogue<F16, EPI>(a, taddr, unit, tile, mb, nb, static_cast<int>(rank), q, lane, abort,
-                                         mapa(tmem_empty(acc), 0));
+                                         mapa(tmem_empty(acc), 0), par);
                 continue;
             }
             if constexpr (EPI == HMB_EPI_SWIGLU) {
@@ -461,7 +474,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                             *reinterpret_cast<float4 *>(y + 8 * g8 + 4) = make_float4(o[4], o[5], o[6], o[7]);
                         }
                     } else if (tok < a.m) {
-                        uint16_t *y = static_cast<uint16_t *>(a.y) + static_cast<int64_t>(tok) * a.ldy + nb * 256 + 32 * cb;
 #pragma unroll
                         for (int g8 = 0; g8 < 4; ++g8) {
                             uint32_t o[4];
@@ -469,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             for (int e = 0; e < 4; ++e)
                                 o[e] = to16<F16>(__uint_as_float(v[8 * g8 + perm_pos(2 * e)])) |
                                        (to16<F16>(__uint_as_float(v[8 * g8 + perm_pos(2 * e + 1)])) << 16);
-                            *reinterpret_cast<uint4 *>(y + 8 * g8) = make_uint4(o[0], o[1], o[2], o[3]);
+                            store_out16(a, par, tok, nb * 256 + 32 * cb + 8 * g8, make_uint4(o[0], o[1], o[2], o[3]));
                         }
                     }
                 }
@@ -478,6 +490,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(mapa(tmem_empty(acc), 0));
         }
+        // Stores into peers' slots are visible at system scope before the boundary kernel that
+        // follows this grid raises its flags.
+        if (a.scatter) __threadfence_system();
     }
 
     fence_before_sync();

@@ -351,8 +351,13 @@ int *device_status_word() {
 
 int gemm_run(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const void *x, int64_t ldx, int x_dtype, void *y, int64_t ldy,
              int y_dtype, int64_t m, int64_t k, int64_t n, int64_t start_col, int epilogue, int layout, void *split_ws, size_t split_ws_bytes,
-             unsigned *split_cnt, cudaStream_t stream) {
-    if (!packed || !x || !y || m <= 0) return HMB_ERR_ARG;
+             unsigned *split_cnt, cudaStream_t stream, const ScatterTarget *sc) {
+    if (!packed || !x || (!y && !sc) || m <= 0) return HMB_ERR_ARG;
+    if (sc && (epilogue != HMB_EPI_STORE || y_dtype == HMB_FP32 || sc->h != n || sc->m != m)) return HMB_ERR_ARG;
+    if (sc) {
+        y = const_cast<void *>(x);  // never written (the rows go to the scatter target); passes the checks below
+        ldy = n;
+    }
     if (k <= 0 || n <= 0 || k % kTileK || n % kTileN || packed_k % kTileK || packed_n % kTileN || start_col < 0 ||
         start_col % kTileN || k > packed_k || start_col + n > packed_n)
         return HMB_ERR_ARG;
@@ -391,7 +396,7 @@ int gemm_run(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const vo
     const bool small_grid = (m + BM - 1) / BM * (n / BN) * 2 < sm_count();
     // or when the pair tiles fit in one round: two SMs per tile, each dequantizing half of it
     const bool one_round = (m + 255) / 256 * (n / 256) <= pair_clusters();
-    if (m > BM || (split_ok && small_grid) || (small_grid && one_round)) {
+    if (m > BM || (split_ok && small_grid) || (small_grid && one_round) || sc) {
         PairArgs p{};
         p.packed = packed;
         p.y = y;
@@ -414,6 +419,10 @@ int gemm_run(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const vo
         p.k_splits = (steps + p.k_per_split - 1) / p.k_per_split;  // no empty split
         p.split_ws = static_cast<float *>(split_ws);
         p.split_cnt = split_cnt;
+        if (sc) {
+            p.scatter = 1;
+            p.sc = *sc;
+        }
         return launch_gemm_pair(map, p, f16, epilogue, stream);
     }
     GemmArgs a{};

@@ -768,6 +768,52 @@ int hmb_w4a16_ffn(const uint8_t *gate_up, const uint8_t *down, int64_t h, int64_
     return HMB_OK;
 }
 
+size_t hmb_tp_ffn_layer_workspace(int64_t m, int64_t h, int64_t n) {
+    const size_t ffn = hmb_w4a16_ffn_workspace(m, h, n);
+    return ffn ? ffn + round256(static_cast<size_t>(m) * h * 2) : 0;
+}
+
+int hmb_tp_ffn_layer(hmb_comm *comm, const uint8_t *gate_up, const uint8_t *down, int64_t h, int64_t n, int64_t stored, int layout,
+                     const void *x, void *resid, const void *norm_weight, float eps, int64_t m, void *workspace, size_t workspace_bytes,
+                     hmb_stream_t stream, uint64_t spin_limit_ns) {
+    if (!comm || !gate_up || !down || !x || !resid || m <= 0) return HMB_ERR_ARG;
+    const size_t ffn_bytes = hmb_w4a16_ffn_workspace(m, h, n);
+    if (!ffn_bytes) return HMB_ERR_ARG;
+    if (!workspace || workspace_bytes < hmb_tp_ffn_layer_workspace(m, h, n)) return HMB_ERR_WORKSPACE;
+    if (!aligned(workspace, 256)) return HMB_ERR_ALIGN;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    void *y = ws + ffn_bytes;  // this rank's partial, when it is not scattered
+
+    // Prefill on two or more ranks: gate/up GEMM with SwiGLU, then the down GEMM storing its partial
+    // rows over NVLink into the receive slots of the boundary, which then only sums and normalises.
+    ScatterTarget t;
+    const bool same_up = layout == HMB_GATE_UP_INTERLEAVED || n == stored;
+    const bool fused = m > 16 && same_up && hmb_w4a16_gemm_supports(m, h, 2 * n, HMB_EPI_SWIGLU) &&
+                       hmb_w4a16_gemm_supports(m, n, h, HMB_EPI_STORE) && comm_scatter_target(comm, m, h, &t) == HMB_OK && t.world > 1;
+    if (fused) {
+        if (h % kTileK || n % kTileK || stored % kTileK || n > stored) return HMB_ERR_ARG;
+        if (layout != HMB_GATE_UP_BLOCKED && layout != HMB_GATE_UP_INTERLEAVED) return HMB_ERR_ARG;
+        if (!aligned(x, 16)) return HMB_ERR_ALIGN;
+        unsigned *gu_split_cnt = reinterpret_cast<unsigned *>(ws + 2 * kCounterBytes);
+        unsigned *dn_split_cnt = reinterpret_cast<unsigned *>(ws + 2 * kCounterBytes + kSplitCounterBytes);
+        uint8_t *act_p = ws + kFfnControlBytes;
+        uint8_t *scratch = act_p + round256(static_cast<size_t>(m) * n * 2);
+        const size_t scratch_bytes = ffn_bytes - (scratch - ws);
+        int rc = gemm_run(gate_up, h, 2 * stored, x, h, HMB_BF16, act_p, n, HMB_BF16, m, h, 2 * n, 0, HMB_EPI_SWIGLU, layout, scratch,
+                          scratch_bytes, gu_split_cnt, s);
+        if (rc != HMB_OK) return rc;
+        rc = gemm_run(down, stored, h, act_p, n, HMB_BF16, nullptr, h, HMB_BF16, m, n, h, 0, HMB_EPI_STORE, 0, scratch, scratch_bytes,
+                      dn_split_cnt, s, &t);
+        if (rc != HMB_OK) return rc;
+        return comm_boundary(comm, nullptr, resid, norm_weight, m, h, eps, true, s, spin_limit_ns);
+    }
+    // Decode (and a group of one): the FFN into y, then the boundary with its own exchange.
+    int rc = hmb_w4a16_ffn(gate_up, down, h, n, stored, layout, x, h, HMB_BF16, y, h, HMB_BF16, m, workspace, ffn_bytes, stream);
+    if (rc != HMB_OK) return rc;
+    return comm_boundary(comm, y, resid, norm_weight, m, h, eps, false, s, spin_limit_ns);
+}
+
 }  // extern "C"
 
 // ---- the GEMV without caller workspace ------------------------------------------------------------------

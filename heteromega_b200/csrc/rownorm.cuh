@@ -13,8 +13,7 @@
 namespace hmb {
 
 constexpr int kRowThreads = 256;
-constexpr int kRowMaxVec = 8;  // 16-byte vectors per thread: rows of up to 8 * 8 * 256 = 16384 values
-constexpr int kRowMaxH = kRowMaxVec * 8 * kRowThreads;
+constexpr int kRowMaxH = 8 * 8 * kRowThreads;  // 8 vectors of 8 values per thread: 16384
 
 // Sum of v over the CTA. Every thread gets the same bits: the warp totals are added in warp order.
 // red: kRowThreads / 32 floats of shared memory; all threads of the CTA must call.
@@ -46,42 +45,63 @@ __device__ __forceinline__ uint4 pack8(const float *f) {
     return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// in[0..n_in): addend rows (bf16, h values). x: the residual row, overwritten with x_new when
-// n_in > 0 and write_x. out[0..n_out): rows that all receive the result. w: the norm weight row or
-// null. h % 8 == 0, h <= kRowMaxH; every pointer 16-byte aligned. All threads of the CTA must call.
-__device__ __forceinline__ void boundary_row(const uint16_t *const *in, int n_in, uint16_t *x, bool write_x, const uint16_t *w,
-                                             int h, float eps, uint16_t *const *out, int n_out, float *red) {
+// Vectors of 8 values per thread for rows of h values: V = 1, 2, 4 or 8 (h <= 2048 V).
+__host__ __device__ constexpr int row_vectors(int64_t h) { return h <= 2048 ? 1 : h <= 4096 ? 2 : h <= 8192 ? 4 : 8; }
+
+// in[0..NIN): addend rows (bf16, h values). x: the residual row, overwritten with x_new when NIN > 0
+// and write_x. out[0..n_out): rows that all receive the result. w: the norm weight row or null.
+// h % 8 == 0, h <= V * 2048; every pointer 16-byte aligned. All threads of the CTA must call.
+// The loads of x and of every addend are issued before the sums (no load waits for an add), so a
+// row costs about one memory latency, not one per addend.
+template <int V, int NIN>
+__device__ __forceinline__ void boundary_row(const uint16_t *const *in, uint16_t *x, bool write_x, const uint16_t *w, int h,
+                                             float eps, uint16_t *const *out, int n_out, float *red) {
     const int nv = h >> 3;
-    uint4 xv[kRowMaxVec];
+    // Vectors in groups of G: every load of a group (x and the addends) is in flight at once, and a
+    // group's loads stay within the registers.
+    constexpr int G = V * (NIN + 1) <= 40 ? V : (40 / (NIN + 1) >= 1 ? 40 / (NIN + 1) : 1);
+    uint4 xv[V];
     float ss = 0.0f;
 #pragma unroll
-    for (int i = 0; i < kRowMaxVec; ++i) {
-        const int v = i * kRowThreads + threadIdx.x;
-        if (v < nv) {
-            uint4 cur = *reinterpret_cast<const uint4 *>(x + 8 * v);
-            if (n_in > 0) {
-                float acc[8];
-                unpack8(cur, acc);
-                for (int r = 0; r < n_in; ++r) {
-                    float p[8];
-                    unpack8(*reinterpret_cast<const uint4 *>(in[r] + 8 * v), p);
+    for (int i0 = 0; i0 < V; i0 += G) {
+        uint4 pv[NIN > 0 ? NIN : 1][G];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) acc[e] += p[e];
-                }
-                cur = pack8(acc);
-                if (write_x) *reinterpret_cast<uint4 *>(x + 8 * v) = cur;
+        for (int j = 0; j < G && i0 + j < V; ++j) {
+            const int v = (i0 + j) * kRowThreads + threadIdx.x;
+            if (v < nv) {
+                xv[i0 + j] = *reinterpret_cast<const uint4 *>(x + 8 * v);
+#pragma unroll
+                for (int r = 0; r < NIN; ++r) pv[r][j] = *reinterpret_cast<const uint4 *>(in[r] + 8 * v);
             }
-            xv[i] = cur;
-            float f[8];
-            unpack8(cur, f);
+        }
 #pragma unroll
-            for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
+        for (int j = 0; j < G && i0 + j < V; ++j) {
+            const int v = (i0 + j) * kRowThreads + threadIdx.x;
+            if (v < nv) {
+                if constexpr (NIN > 0) {
+                    float acc[8];
+                    unpack8(xv[i0 + j], acc);
+#pragma unroll
+                    for (int r = 0; r < NIN; ++r) {
+                        float p[8];
+                        unpack8(pv[r][j], p);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) acc[e] += p[e];
+                    }
+                    xv[i0 + j] = pack8(acc);
+                    if (write_x) *reinterpret_cast<uint4 *>(x + 8 * v) = xv[i0 + j];
+                }
+                float f[8];
+                unpack8(xv[i0 + j], f);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
+            }
         }
     }
     float scale = 1.0f;
     if (w != nullptr) scale = rsqrtf(cta_sum(ss, red) / static_cast<float>(h) + eps);
 #pragma unroll
-    for (int i = 0; i < kRowMaxVec; ++i) {
+    for (int i = 0; i < V; ++i) {
         const int v = i * kRowThreads + threadIdx.x;
         if (v < nv) {
             uint4 o = xv[i];

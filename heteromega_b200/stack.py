@@ -10,8 +10,10 @@ layer's input). FfnStack keeps exactly that chain for the FFN layers alone:
     result = h_L
 
 With a TensorParallelFfn the layers are this rank's shards: FFN_l gives this rank's partial and
-the boundary sums the partials of all ranks too (the NVLink kernel hmb_allreduce_residual_norm,
-or NCCL followed by hmb_residual_norm). On B200 a decode layer takes a few microseconds, so the
+the boundary sums the partials of all ranks too. On the NVLink communicator one call runs the layer
+(hmb_tp_ffn_layer: for prefill the down GEMM stores its partial rows straight into the peers'
+receive slots and the boundary kernel sums, normalises and gathers); with NCCL the partial is
+all-reduced and hmb_residual_norm follows. On B200 a decode layer takes a few microseconds, so the
 stack captures the whole chain for a given M once and replays it.
 """
 import torch
@@ -53,13 +55,16 @@ class FfnStack:
         h, y, x = b["h"], b["y"], b["x"]
         h.copy_(h_in)
         L = len(self.layers)
-        if self.tp is not None and self.tp.comm is not None and self.tp.world > 1 and self.tp.collective == "hmb":
+        fused = self.tp is not None and self.tp.comm is not None and self.tp.world > 1 and self.tp.collective == "hmb"
+        if fused:
             x = self.tp.comm.out(m, self.hidden)  # the boundary's output region, the next layer's input
         ops.residual_norm(h, None, None, self.norms[0], x, self.eps)
         for l in range(L):
             last = l == L - 1
             g = None if last else self.norms[l + 1]
-            if self.tp is None:
+            if fused:
+                out = self.tp.layer(l, x, h, g, self.eps)
+            elif self.tp is None:
                 w: FfnSliceWeights = self.layers[l]
                 ops.w4a16_ffn(y, x, w.gate_up, w.down, w.hidden, w.channels(), w.stored_channels(), int(w.layout))
                 ops.residual_norm(h, y, None, g, None if last else x, self.eps)

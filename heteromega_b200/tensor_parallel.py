@@ -19,7 +19,7 @@ from . import _lib
 from ._lib import check, lib
 from .gpu_ffn import FfnSliceWeights, GateUpLayout, slice_packed_ffn
 from .partition import plan_shards
-from .torch_ops import ops
+from .torch_ops import ops, workspace
 
 
 class PeerComm:
@@ -187,6 +187,27 @@ class TensorParallelFfn:
             return h
         ops.residual_norm(h, partial, None, weight, normed, eps)
         return normed
+
+    def layer(self, layer, x, h, weight, eps, spin_limit_ns=0):
+        """One whole layer with its boundary on the NVLink communicator (hmb_tp_ffn_layer): this rank's
+        partial of FFN `layer` for x [m, H], summed over the ranks into h's kept rows, and the next
+        input RMSNorm(h) * weight (h itself without weight) in the output region, whose view it
+        returns. For m > 16 the down GEMM writes its partial rows straight into the peers' slots."""
+        if self.comm is None:
+            raise RuntimeError("TensorParallelFfn: call connect(max_rows, device) on every rank first")
+        w = self.layers[layer]
+        m = x.shape[0]
+        for name, t in (("x", x), ("h", h)):
+            if t.dtype != torch.bfloat16 or not t.is_contiguous() or tuple(t.shape) != (m, self.hidden):
+                raise ValueError(f"TensorParallelFfn.layer: {name} must be contiguous bf16 [m, hidden]")
+        nbytes = lib().hmb_tp_ffn_layer_workspace(m, w.hidden, w.channels())
+        ws = workspace(h.device, nbytes, kind="tp_layer")
+        check(lib().hmb_tp_ffn_layer(self.comm._ptr, w.gate_up.data_ptr(), w.down.data_ptr(), w.hidden, w.channels(),
+                                     w.stored_channels(), int(w.layout), x.data_ptr(), h.data_ptr(),
+                                     weight.data_ptr() if weight is not None else None, float(eps), m, ws.data_ptr(),
+                                     ws.numel(), torch.cuda.current_stream(h.device).cuda_stream, spin_limit_ns),
+              "hmb_tp_ffn_layer")
+        return self.comm.out(m, self.hidden)
 
     def forward(self, layer, x, y):
         """y[m, H] (x's dtype) = the whole FFN layer for x, on every rank: this rank's partial written

@@ -207,6 +207,22 @@ int hmb_comm_destroy(hmb_comm *comm);
  * HMB_ERR_TIMEOUT in the device status word. A group of one runs hmb_residual_norm into the output. */
 int hmb_allreduce_residual_norm(const void *y, void *x, const void *weight, int64_t m, int64_t h, float eps, hmb_comm *comm,
                                 hmb_stream_t stream, uint64_t spin_limit_ns);
+/* One tensor-parallel FFN layer with its boundary, end to end on this rank: this rank's channel slice
+ * of the layer (as hmb_w4a16_ffn: gate_up, down, h, n, stored, layout) for x[m, h] (bf16, ld = h;
+ * normally the output region holding the previous boundary's result), then the boundary of
+ * hmb_allreduce_residual_norm on resid[m, h] with norm_weight (null: no norm) into the output region.
+ * For m > 16 on two or more ranks the down GEMM stores its partial rows over NVLink straight into
+ * the receive slots the boundary reads (the owner's rows, or every rank's for one-shot sizes), so
+ * the reduce-scatter overlaps the GEMM tile by tile and the boundary only sums, normalises and
+ * gathers; otherwise the partial goes to the workspace and the boundary exchanges it. workspace:
+ * hmb_tp_ffn_layer_workspace(m, h, n) bytes, 256-byte aligned, zero-filled once before the first call.
+ * Replaces, per layer, GpuFfnModel::forward plus the boundary of the model loop
+ * (kernels/gpu/src/gpu_ffn.cpp:142-156; src/unified_llm_w4a16_hetero/unified_llm_w4a16.cpp:2533-2540,
+ * 2852-2865) with the partner device's partial coming from the other ranks. */
+int hmb_tp_ffn_layer(hmb_comm *comm, const uint8_t *gate_up, const uint8_t *down, int64_t h, int64_t n, int64_t stored, int layout,
+                     const void *x, void *resid, const void *norm_weight, float eps, int64_t m, void *workspace, size_t workspace_bytes,
+                     hmb_stream_t stream, uint64_t spin_limit_ns);
+size_t hmb_tp_ffn_layer_workspace(int64_t m, int64_t h, int64_t n);
 /* The output region of hmb_allreduce_residual_norm: *ptr (256-byte aligned), *bytes = max_bytes. */
 int hmb_comm_out(hmb_comm *comm, void **ptr, size_t *bytes);
 /* Rows [*begin, *end) of an m x h boundary whose residual this rank keeps (all rows when one-shot). */

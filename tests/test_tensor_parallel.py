@@ -144,11 +144,29 @@ def _gpu_rank(rank, world, port, out_path, collective):
         from heteromega_b200.stack import FfnStack
 
         norms = [(torch.randn(hidden, device=dev, generator=gen) * 0.2 + 1.0).to(torch.bfloat16) for _ in range(2)]
+        if collective == "hmb":
+            # The fused layer (down GEMM scattering its rows into the peers' slots) against the same
+            # layer unfused (partial in local memory, then the exchanging boundary): the same bits,
+            # at a one-shot size (100 rows) and a two-shot size (300 rows).
+            fused_same = []
+            for m in (100, 300):
+                gen.manual_seed(60 + m)
+                x = torch.randn(m, hidden, device=dev, generator=gen).to(torch.bfloat16)
+                h_res = torch.randn(m, hidden, device=dev, generator=gen).to(torch.bfloat16)
+                h1, h2 = h_res.clone(), h_res.clone()
+                out1 = tp.layer(0, x, h1, norms[0], 1e-5).clone()
+                part = torch.empty(m, hidden, dtype=torch.bfloat16, device=dev)
+                tp.local_partial(0, x, part)
+                out2 = tp.comm.boundary(part, h2, norms[0], 1e-5).clone()
+                torch.cuda.synchronize()
+                b, e = tp.comm.rows(m, hidden)
+                fused_same.append(bool(torch.equal(out1, out2)) and bool(torch.equal(h1[b:e], h2[b:e])))
+            res["fused_same"] = np.array(all(fused_same))
         tp.add_layer(g, u, d)  # a second layer (the same weights)
         st_tp = FfnStack(None, hidden, dev, tp=tp, norms=norms)
         st_one = FfnStack([full, full], hidden, dev, norms=norms)
         same = []
-        for m in (1, 300):
+        for m in (1, 100, 300):
             gen.manual_seed(40 + m)
             h0 = torch.randn(m, hidden, device=dev, generator=gen).to(torch.bfloat16)
             got, ref = torch.empty_like(h0), torch.empty_like(h0)
@@ -269,5 +287,7 @@ def test_two_gpus(tmp_path, collective):
         for m in (1, 7, 300, 1024):
             assert_close(r[f"got{m}"], r[f"ref{m}"], LEVEL, f"TP2 {collective} vs single GPU m={m} rank {rank}")
         assert bool(r["stack_graph_same"])
-        for m in (1, 300):
+        if collective == "hmb":
+            assert bool(r["fused_same"]), "the scattering down GEMM must give the unfused layer's bits"
+        for m in (1, 100, 300):
             assert_close(r[f"stack{m}"], r[f"stackref{m}"], LEVEL, f"TP2 {collective} chained stack m={m} rank {rank}")
