@@ -302,7 +302,8 @@ def run_hmb(args):
     else:
         achieved = dom["flops"] / (dom["ms"] * 1e-3) / 1e12
         roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-                "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": traffic_from_profiles(wl, "gate_up")}
+                "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": traffic_from_profiles(wl, "gate_up"),
+                "frac_of_sustained": round(achieved / pk["bf16_tflops_sustained"], 4)}
     roof["peak_source"] = f"of {pk_kind}"
     roof["kernel"] = dom["name"]
     roof["kernel_ms"] = round(dom["ms"], 5)
