@@ -21,7 +21,8 @@ struct PairArgs {
     int m_blocks;    // ceil(M / 256)
     int n_blocks;    // N / 256
     int num_tiles;   // m_blocks x n_blocks
-    int cols_fastest;  // tile order: column blocks fastest (x larger than the weights) or row blocks
+    int band_rows;   // tile order: bands of `band` row blocks (1) or of `band` column blocks (0)
+    int band;
     int col_stride;  // SwiGLU blocked layout: tile columns from gate to up; 1 = interleaved
     int y_f32;       // HMB_EPI_STORE: write the fp32 sums instead of rounding them
     int *status;     // device status word (1 after a wait gave up)
@@ -32,6 +33,10 @@ struct PairArgs {
     int scatter;          // HMB_EPI_STORE, 16-bit output: rows go to the communicator's receive slots `sc`
     ScatterTarget sc;
 };
+
+// The band order of an m x k x n problem (m_blocks x n_blocks tiles of 256 x 256): the direction
+// and width that read the fewest bytes from DRAM when a band of one operand stays in L2.
+void pair_band_order(int64_t m, int64_t k, int64_t n, int *band_rows, int *band);
 
 // CTA pairs the pair kernel keeps resident on the current device.
 int pair_clusters();

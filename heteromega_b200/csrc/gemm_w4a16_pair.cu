@@ -225,10 +225,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int num_units = a.num_tiles * a.k_splits;
     auto unit_k0 = [&](int u) { return (u % a.k_splits) * a.k_per_split; };
     auto unit_k1 = [&](int u) { return min(num_k, unit_k0(u) + a.k_per_split); };
-    // Tile t -> (row block, column block): the operand that is larger in bytes stays resident in L2
-    // while the other one streams (column blocks fastest when x is the larger one).
-    auto tile_mb = [&](int t) { return a.cols_fastest ? t / a.n_blocks : t % a.m_blocks; };
-    auto tile_nb = [&](int t) { return a.cols_fastest ? t % a.n_blocks : t / a.m_blocks; };
+    // Tile t -> (row block, column block) in bands: a band of `band` row blocks (band_rows) whose x
+    // stays in L2 while the column blocks of the weights stream past it, row blocks fastest inside
+    // the band; or the mirror image with a band of column blocks. The pairs working at one time hold
+    // consecutive tiles, so each weight (or x) block comes from DRAM about once per band.
+    auto tile_mb = [&](int t) {
+        const int per = a.band * (a.band_rows ? a.n_blocks : a.m_blocks), b = t / per, i = t - b * per;
+        const int g = min(a.band, (a.band_rows ? a.m_blocks : a.n_blocks) - b * a.band);
+        return a.band_rows ? b * a.band + i % g : i / g;
+    };
+    auto tile_nb = [&](int t) {
+        const int per = a.band * (a.band_rows ? a.n_blocks : a.m_blocks), b = t / per, i = t - b * per;
+        const int g = min(a.band, (a.band_rows ? a.m_blocks : a.n_blocks) - b * a.band);
+        return a.band_rows ? i / g : b * a.band + i % g;
+    };
 
     // Tile column d (0..3) of pair tile column nb, relative to the packed matrix. SwiGLU keeps them
     // as [gate, up, gate, up] of two 64-channel blocks.
@@ -594,6 +604,20 @@ size_t pair_split_bytes(int64_t m, int64_t k, int64_t n) {
     if (splits <= 1) return 0;
     const int64_t tiles = (m + 255) / 256 * (n / 256);
     return static_cast<size_t>(tiles * splits * 2) * 128 * 256 * sizeof(float) + static_cast<size_t>(tiles * 2 * 2) * 4 + 256;
+}
+
+void pair_band_order(int64_t m, int64_t k, int64_t n, int *band_rows, int *band) {
+    // A band of one operand kept in L2 (budget well under the 126 MB: the other operand streams
+    // through the same cache); DRAM bytes ~ that operand once + the other once per band.
+    constexpr double kBudget = 48.0 * 1024 * 1024;
+    const int64_t mb = (m + 255) / 256, nb = n / 256;
+    const double xrow = 256.0 * k * 2, wcol = static_cast<double>(k) * 256 * kTileBytes / (kTileK * kTileN);
+    const int64_t gm = std::max<int64_t>(1, std::min<int64_t>(mb, static_cast<int64_t>(kBudget / xrow)));
+    const int64_t gn = std::max<int64_t>(1, std::min<int64_t>(nb, static_cast<int64_t>(kBudget / wcol)));
+    const double rows = mb * xrow + static_cast<double>((mb + gm - 1) / gm) * nb * wcol;
+    const double cols = nb * wcol + static_cast<double>((nb + gn - 1) / gn) * mb * xrow;
+    *band_rows = rows <= cols;
+    *band = static_cast<int>(rows <= cols ? gm : gn);
 }
 
 int launch_gemm_pair(const CUtensorMap &map, const PairArgs &a, bool f16, int epilogue, cudaStream_t stream) {

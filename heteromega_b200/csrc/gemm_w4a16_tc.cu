@@ -409,7 +409,7 @@ int gemm_run(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const vo
         p.m_blocks = static_cast<int>((m + 255) / 256);
         p.n_blocks = static_cast<int>(n / 256);
         p.num_tiles = p.m_blocks * p.n_blocks;
-        p.cols_fastest = m * k * 2 > k * n * kTileBytes / (kTileK * kTileN);
+        pair_band_order(m, k, n, &p.band_rows, &p.band);
         p.col_stride = col_stride;
         p.y_f32 = y_dtype == HMB_FP32;
         p.status = status;
