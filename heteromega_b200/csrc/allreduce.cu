@@ -248,8 +248,12 @@ __global__ void __launch_bounds__(kThreads, 1) allreduce_kernel(const ArArgs a) 
     const uint8_t *in[kMaxRanks];
 
     if (!a.two_shot) {
-        // One-shot: this rank's message into every rank's slot[me]; then sum the P slots here.
-        for (int r = 0; r < l.world; ++r) copy_blocks(slot(l, r, 0, par, l.rank), y, bytes);
+        // One-shot: this rank's message into every rank's slot[me]; then sum the P slots here. Each
+        // rank visits the peers starting after itself, so no GPU receives from all ranks at once.
+        for (int j = 0; j < l.world; ++j) {
+            const int r = (l.rank + j) % l.world;
+            copy_blocks(slot(l, r, 0, par, l.rank), y, bytes);
+        }
         if (!exchange_flags(l, 0, par, epoch, &s_ok)) return;
         for (int r = 0; r < l.world; ++r) in[r] = slot(l, l.rank, 0, par, r);
         sum_blocks<T>(l.world, y, in, bytes);
@@ -260,7 +264,10 @@ __global__ void __launch_bounds__(kThreads, 1) allreduce_kernel(const ArArgs a) 
     const int64_t chunk = ((bytes + l.world - 1) / l.world + 15) / 16 * 16;
     auto chunk_bytes = [&](int c) { return std::max<int64_t>(0, std::min<int64_t>(chunk, bytes - c * chunk)); };
     // Reduce-scatter: chunk c of this rank's message into rank c's slot[me].
-    for (int c = 0; c < l.world; ++c) copy_blocks(slot(l, c, 0, par, l.rank), y + c * chunk, chunk_bytes(c));
+    for (int j = 0; j < l.world; ++j) {
+        const int c = (l.rank + j) % l.world;
+        copy_blocks(slot(l, c, 0, par, l.rank), y + c * chunk, chunk_bytes(c));
+    }
     if (!exchange_flags(l, 0, par, epoch, &s_ok)) return;
     // The sum of this rank's chunk, in rank order, into this rank's gather slot[me], then into every
     // other rank's gather slot[me].
@@ -268,8 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1) allreduce_kernel(const ArArgs a) 
     for (int r = 0; r < l.world; ++r) in[r] = slot(l, l.rank, 0, par, r);
     sum_blocks<T>(l.world, mine, in, chunk_bytes(l.rank));
     __syncthreads();
-    for (int r = 0; r < l.world; ++r)
-        if (r != l.rank) copy_blocks(slot(l, r, 1, par, l.rank), mine, chunk_bytes(l.rank));
+    for (int j = 1; j < l.world; ++j) copy_blocks(slot(l, (l.rank + j) % l.world, 1, par, l.rank), mine, chunk_bytes(l.rank));
     if (!exchange_flags(l, 1, par, epoch, &s_ok)) return;
     // Gather: chunk c from gather slot[c] into y.
     for (int c = 0; c < l.world; ++c) copy_blocks(y + c * chunk, slot(l, l.rank, 1, par, c), chunk_bytes(c));
@@ -298,8 +304,7 @@ __global__ void __launch_bounds__(kThreads, 1) boundary_kernel(const BnArgs a) {
     const bool own_y = !a.prefilled;
     if (!a.two_shot) {
         if (!a.prefilled)
-            for (int r = 0; r < l.world; ++r)
-                if (r != l.rank) copy_blocks(slot(l, r, 0, par, l.rank), y, a.m * row_bytes);
+            for (int j = 1; j < l.world; ++j) copy_blocks(slot(l, (l.rank + j) % l.world, 0, par, l.rank), y, a.m * row_bytes);
         raise_flags(l, 0, par, epoch);
         if (!wait_all_ctas(l, 0, par, epoch, &s_ok)) return;
         for (int64_t row = blockIdx.x; row < a.m; row += kCtas) {
@@ -315,9 +320,10 @@ __global__ void __launch_bounds__(kThreads, 1) boundary_kernel(const BnArgs a) {
 
     // Reduce-scatter by rows: rank c's rows of this rank's partial into rank c's slot[me].
     if (!a.prefilled)
-        for (int c = 0; c < l.world; ++c) {
+        for (int j = 1; j < l.world; ++j) {  // owners visited from the next rank on: no incast
+            const int c = (l.rank + j) % l.world;
             const int64_t r0 = comm_share_row(a.m, l.world, c), r1 = comm_share_row(a.m, l.world, c + 1);
-            if (c != l.rank) copy_blocks(slot(l, c, 0, par, l.rank), y + r0 * row_bytes, (r1 - r0) * row_bytes);
+            copy_blocks(slot(l, c, 0, par, l.rank), y + r0 * row_bytes, (r1 - r0) * row_bytes);
         }
     raise_flags(l, 0, par, epoch);
     if (!wait_all_ctas(l, 0, par, epoch, &s_ok)) return;

@@ -229,10 +229,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     // stays in L2 while the column blocks of the weights stream past it, row blocks fastest inside
     // the band; or the mirror image with a band of column blocks. The pairs working at one time hold
     // consecutive tiles, so each weight (or x) block comes from DRAM about once per band.
+    // Scattering to row owners, every rank starts its row blocks at its own offset (rank * m_blocks
+    // / P): at any moment rank r stores to a different owner than the other ranks, instead of all
+    // ranks pouring their rows into the same one or two GPUs.
+    const int mb_shift = a.scatter && !a.sc.all ? static_cast<int>(static_cast<int64_t>(a.sc.rank) * a.m_blocks / a.sc.world) : 0;
     auto tile_mb = [&](int t) {
         const int per = a.band * (a.band_rows ? a.n_blocks : a.m_blocks), b = t / per, i = t - b * per;
         const int g = min(a.band, (a.band_rows ? a.m_blocks : a.n_blocks) - b * a.band);
-        return a.band_rows ? b * a.band + i % g : i / g;
+        const int mb = a.band_rows ? b * a.band + i % g : i / g;
+        return mb_shift ? (mb + mb_shift) % a.m_blocks : mb;
     };
     auto tile_nb = [&](int t) {
         const int per = a.band * (a.band_rows ? a.n_blocks : a.m_blocks), b = t / per, i = t - b * per;
