@@ -12,7 +12,11 @@ test time; the GPU box never sees the reference tree.
 
 Reference code used (paths inside glassescrab/HeteroMega):
   py/unified_llm_w4a16/llama3_8b_w4a16_model.py   _pack_weights_packed (546-656),
-                                                  _unpack_awq_qweight/_qzeros (340-358)
+                                                  _unpack_awq_qweight/_qzeros (340-358),
+                                                  the pre-saved weight directory: _write_tensor_raw (318-322),
+                                                  _pack_qweight_out_in2 (410-419), _split_packed_paths
+                                                  (460-465), _split_packed_bin_from_file (468-529),
+                                                  the manifest keys (962-978) and file names (1069-1168)
   kernels/gpu/tools/check_packing.py              pack (53-69), gemv_packed (91-112)
   experiments/ffn_partition/gpu_backend.py        pack_heteromosaic_weights (33-77)
   experiments/ffn_partition/test_gpu_packing.py   decode_gpu_addresses (18-43)
@@ -202,14 +206,74 @@ def make_slices():
     np.savez_compressed(os.path.join(HERE, "slices.npz"), **out)
 
 
+def make_checkpoint():
+    """Three pre-saved weight directories of a 2-layer FFN (hidden 128, intermediate 384), written by
+    the reference's own functions: packed bins (down split along K at 256 into its .k256.packed0/1
+    pair; layer 0 with the older untagged .packed0/1 names), layer 0 padded to multiples of 2048 (pad_packed_weights), and the
+    unpacked qweight/scales/zeros bins. The fixture keeps every file's bytes and the q/s/z drawn."""
+    import json
+    import tempfile
+    from pathlib import Path
+
+    hidden, inter, layers = 128, 384, 2
+    specs = [("gate", hidden, inter), ("up", hidden, inter), ("down", inter, hidden)]
+    out = {"hidden": hidden, "inter": inter, "layers": layers}
+    weights = {}
+    for l in range(layers):
+        for name, k, n in specs:
+            q, s, z = quant(rng(500 + 10 * l + len(name)), k, n)
+            weights[(l, name)] = (q, s, z)
+            out[f"src_{l}_{name}_q"], out[f"src_{l}_{name}_s"], out[f"src_{l}_{name}_z"] = q, bits(s).astype(np.uint16), z
+    for tag, use_packed, pad in (("packed", True, False), ("padded", True, True), ("unpacked", False, False)):
+        with tempfile.TemporaryDirectory() as d:
+            d = Path(d)
+            split = {"down": 256} if tag == "packed" else {}
+            n_layers = 1 if pad else layers  # the padded files are 2048 x 2048: one layer is enough
+            for l in range(n_layers):
+                for name, k, n in specs:
+                    q, s, z = weights[(l, name)]
+                    if use_packed:
+                        packed = hm_model._pack_weights_packed(torch.from_numpy(q.astype(np.int8)),
+                                                               torch.from_numpy(s).to(torch.bfloat16),
+                                                               torch.from_numpy(z.astype(np.int8)), k, n, pad)
+                        path = d / f"layer_{l}_{name}.packed.bin"
+                        hm_model._write_tensor_raw(path, packed)
+                        if name in split:  # split_k_by_layer applies to this projection of every layer
+                            p0, p1 = hm_model._split_packed_paths(d, l, name, split[name])
+                            assert hm_model._split_packed_bin_from_file(path, p0, p1, split[name], k, n, pad)
+                            path.unlink()  # only the split pair stays, as the split writer leaves it
+                            if l == 0:  # the untagged names of older directories, which the C++ loader accepts
+                                p0.rename(d / f"layer_{l}_{name}.packed0.bin")
+                                p1.rename(d / f"layer_{l}_{name}.packed1.bin")
+                    else:
+                        hm_model._write_tensor_raw(d / f"layer_{l}_{name}.qweight.bin",
+                                                   hm_model._pack_qweight_out_in2(torch.from_numpy(q.astype(np.int8))))
+                        # [out, groups], the layout the unpacked writer normalises to
+                        # [out, groups] row-major (passed flat: the bytes are the same)
+                        hm_model._write_tensor_raw(d / f"layer_{l}_{name}.scales.bin",
+                                                   torch.from_numpy(s.T.copy().ravel()).to(torch.bfloat16))
+                        hm_model._write_tensor_raw(d / f"layer_{l}_{name}.zeros.bin",
+                                                   torch.from_numpy(z.T.copy().ravel().astype(np.int8)))
+            manifest = {"format_version": 1, "model_name": "tiny-ffn", "use_packed_weights": use_packed,
+                        "pad_packed_weights": pad, "heterogeneity": "gpu",
+                        "split_k_by_layer": split if use_packed else {}, "num_hidden_layers": n_layers,
+                        "hidden_size": hidden, "intermediate_size": inter, "num_attention_heads": 2,
+                        "num_key_value_heads": 2, "head_dim": 128, "groupsize": 128}
+            if not use_packed:
+                manifest["unpacked_layout"] = "out_groups_v2"
+            (d / "manifest.json").write_text(json.dumps(manifest, indent=2))
+            names = sorted(f.name for f in d.iterdir())
+            out[f"{tag}_files"] = np.array(names)
+            for f in names:
+                out[f"{tag}/{f}"] = np.frombuffer((d / f).read_bytes(), np.uint8)
+    np.savez_compressed(os.path.join(HERE, "checkpoint.npz"), **out)
+
+
 if __name__ == "__main__":
-    make_packing()
-    make_awq()
-    make_gemv()
-    make_ffn()
-    make_contract()
-    make_bf16()
-    make_slices()
+    only = sys.argv[1:]
+    for fn in (make_packing, make_awq, make_gemv, make_ffn, make_contract, make_bf16, make_slices, make_checkpoint):
+        if not only or fn.__name__ in only:
+            fn()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

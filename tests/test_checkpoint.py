@@ -1,0 +1,100 @@
+"""The reference's pre-saved weight directory (its on-disk FFN format) read by heteromega_b200.checkpoint.
+
+tests/golden/checkpoint.npz holds three directories of a 2-layer FFN written by the reference's own
+functions (tests/golden/make_golden.py: _pack_weights_packed, _write_tensor_raw,
+_split_packed_bin_from_file, _pack_qweight_out_in2): packed bins with one projection split along K,
+the 2048-padded variant, and the unpacked qweight/scales/zeros bins. Every matrix read back must be
+byte-identical to the host packer's output for the same q/s/z (the packer itself is pinned to the
+reference's packers by test_oracle_golden), and shards cut at load time to slice_packed_ffn's.
+"""
+import json
+
+import numpy as np
+import pytest
+import torch
+
+import heteromega_b200 as H
+from heteromega_b200.checkpoint import Checkpoint, CheckpointError, load_ffn_stack, tile_positions
+from heteromega_b200.partition import plan_shards
+from heteromega_b200.tensor_parallel import TensorParallelFfn
+
+
+@pytest.fixture(scope="module")
+def ck_npz(golden):
+    return golden("checkpoint")
+
+
+def materialize(npz, tag, root):
+    d = root / tag
+    d.mkdir()
+    for f in npz[f"{tag}_files"]:
+        (d / str(f)).write_bytes(npz[f"{tag}/{f}"].tobytes())
+    return d
+
+
+def expected(npz, layer, name):
+    q = torch.from_numpy(npz[f"src_{layer}_{name}_q"])
+    s = torch.from_numpy(npz[f"src_{layer}_{name}_s"].view(np.int16)).view(torch.bfloat16)
+    z = torch.from_numpy(npz[f"src_{layer}_{name}_z"])
+    return H.pack_w4a16(q, s, z)
+
+
+@pytest.mark.parametrize("tag", ["packed", "padded", "unpacked"])
+def test_matrices_match_the_packer(ck_npz, tmp_path, tag):
+    ck = Checkpoint(materialize(ck_npz, tag, tmp_path))
+    assert (ck.hidden, ck.inter) == (int(ck_npz["hidden"]), int(ck_npz["inter"]))
+    for layer in range(ck.layers):
+        for name in ("gate", "up", "down"):
+            got = ck.matrix(layer, name)
+            assert torch.equal(got, expected(ck_npz, layer, name)), f"{tag} layer {layer} {name}"
+    if tag == "packed":
+        assert ck.split_k == {"down": 256}
+        assert not (ck.path / "layer_1_down.packed.bin").exists()  # read from the .k256 split pair
+        assert (ck.path / "layer_0_down.packed0.bin").exists()  # and from the untagged pair
+
+
+def test_shards_match_slices(ck_npz, tmp_path):
+    d = materialize(ck_npz, "packed", tmp_path)
+    ck = Checkpoint(d)
+    for world in (1, 3):
+        for begin, end in plan_shards(ck.inter, world):
+            for layer in range(ck.layers):
+                got = ck.ffn_slice(layer, begin, end)
+                g, u, dn = (expected(ck_npz, layer, n) for n in ("gate", "up", "down"))
+                ref = H.slice_packed_ffn(g, u, dn, ck.hidden, ck.inter, begin, end, H.GateUpLayout.kInterleaved)
+                assert torch.equal(got.gate_up, ref.gate_up) and torch.equal(got.down, ref.down)
+    # a tensor-parallel rank keeps only its shard
+    tp = TensorParallelFfn(ck.hidden, ck.inter, rank=1, world=3)
+    ws = load_ffn_stack(d, "cpu", tp=tp)
+    assert len(tp.layers) == ck.layers and ws[0].channels() == tp.end - tp.begin
+
+
+def test_tile_positions_follow_the_layout():
+    for k, n in ((128, 64), (256, 640), (384, 1152), (1024, 192)):
+        pos = tile_positions(k, n)
+        tk, tn = k // 128, n // 64
+        for c in range(tn):
+            for r in range(tk):
+                assert pos[c, r] == H.packed_tile_index(c, r, tk, tn)
+
+
+def test_rejects_bad_directories(ck_npz, tmp_path):
+    d = materialize(ck_npz, "packed", tmp_path)
+    with pytest.raises(CheckpointError):
+        Checkpoint(tmp_path / "nowhere")
+    m = json.loads((d / "manifest.json").read_text())
+    (d / "manifest.json").write_text(json.dumps(dict(m, format_version=2)))
+    with pytest.raises(CheckpointError, match="format_version"):
+        Checkpoint(d)
+    (d / "manifest.json").write_text(json.dumps(dict(m, split_k_by_layer={"down": 200})))
+    with pytest.raises(CheckpointError, match="split"):
+        Checkpoint(d).matrix(1, "down")
+    (d / "manifest.json").write_text(json.dumps(m))
+    (d / "layer_0_up.packed.bin").write_bytes(b"\\0" * 100)
+    with pytest.raises(CheckpointError, match="bytes"):
+        Checkpoint(d).matrix(0, "up")
+    (d / "layer_0_gate.packed.bin").unlink()
+    with pytest.raises(CheckpointError, match="missing"):
+        Checkpoint(d).matrix(0, "gate")
+    with pytest.raises(CheckpointError, match="no layer"):
+        Checkpoint(d).matrix(5, "gate")
