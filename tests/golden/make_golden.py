@@ -46,6 +46,7 @@ import gpu_backend  # noqa: E402
 import reference  # noqa: E402
 import test_gpu_packing  # noqa: E402
 import llama3_8b_w4a16_model as hm_model  # noqa: E402
+import qwen25_14b_w4a16_model as qwen_model  # noqa: E402
 
 from oracle import oracle as O  # noqa: E402
 
@@ -217,6 +218,8 @@ def make_checkpoint():
 
     hidden, inter, layers = 128, 384, 2
     specs = [("gate", hidden, inter), ("up", hidden, inter), ("down", inter, hidden)]
+    # one attention head and one KV head of 128: q, k, v [128, 128], o [128, 128], fused qkv [128, 384]
+    attn = [("q", hidden, 128), ("k", hidden, 128), ("v", hidden, 128), ("o", 128, hidden)]
     out = {"hidden": hidden, "inter": inter, "layers": layers}
     weights = {}
     for l in range(layers):
@@ -224,6 +227,10 @@ def make_checkpoint():
             q, s, z = quant(rng(500 + 10 * l + len(name)), k, n)
             weights[(l, name)] = (q, s, z)
             out[f"src_{l}_{name}_q"], out[f"src_{l}_{name}_s"], out[f"src_{l}_{name}_z"] = q, bits(s).astype(np.uint16), z
+    for name, k, n in attn:
+        q, s, z = quant(rng(600 + len(name) + ord(name[0])), k, n)
+        weights[(0, name)] = (q, s, z)
+        out[f"src_0_{name}_q"], out[f"src_0_{name}_s"], out[f"src_0_{name}_z"] = q, bits(s).astype(np.uint16), z
     for tag, use_packed, pad in (("packed", True, False), ("padded", True, True), ("unpacked", False, False)):
         with tempfile.TemporaryDirectory() as d:
             d = Path(d)
@@ -254,11 +261,18 @@ def make_checkpoint():
                                                    torch.from_numpy(s.T.copy().ravel()).to(torch.bfloat16))
                         hm_model._write_tensor_raw(d / f"layer_{l}_{name}.zeros.bin",
                                                    torch.from_numpy(z.T.copy().ravel().astype(np.int8)))
+            if tag == "packed":  # layer 0's attention projections, separate and fused (q|k|v columns)
+                for name, k, n in attn:
+                    q, s, z = weights[(0, name)]
+                    hm_model._write_tensor_raw(d / f"layer_0_{name}.packed.bin", torch.from_numpy(torch_pack(q, s, z)))
+                qs = [weights[(0, nm)] for nm in ("q", "k", "v")]
+                cat = [np.concatenate([w[i] for w in qs], axis=1) for i in range(3)]
+                hm_model._write_tensor_raw(d / "layer_0_qkv.packed.bin", torch.from_numpy(torch_pack(*cat)))
             manifest = {"format_version": 1, "model_name": "tiny-ffn", "use_packed_weights": use_packed,
                         "pad_packed_weights": pad, "heterogeneity": "gpu",
                         "split_k_by_layer": split if use_packed else {}, "num_hidden_layers": n_layers,
-                        "hidden_size": hidden, "intermediate_size": inter, "num_attention_heads": 2,
-                        "num_key_value_heads": 2, "head_dim": 128, "groupsize": 128}
+                        "hidden_size": hidden, "intermediate_size": inter, "num_attention_heads": 1,
+                        "num_key_value_heads": 1, "head_dim": 128, "groupsize": 128}
             if not use_packed:
                 manifest["unpacked_layout"] = "out_groups_v2"
             (d / "manifest.json").write_text(json.dumps(manifest, indent=2))
@@ -266,6 +280,33 @@ def make_checkpoint():
             out[f"{tag}_files"] = np.array(names)
             for f in names:
                 out[f"{tag}/{f}"] = np.frombuffer((d / f).read_bytes(), np.uint8)
+    # The Qwen writer's variant (qwen25_14b_w4a16_model.py:1230-1253, 1467-1512): format_version 2 with a
+    # fused qkv bin, padding given as a (K, N) alignment pair and overridden per projection.
+    pad_default, pad_by = (256, 512), {"down": [512, 0], "qkv": [0, 0]}
+    with tempfile.TemporaryDirectory() as d:
+        d = Path(d)
+        for name, k, n in specs + attn[3:]:
+            q, s, z = weights[(0, name)]
+            spec = qwen_model._resolve_layer_pad_packed_alignment(pad_default, {a: tuple(b) for a, b in pad_by.items()}, name)
+            packed = qwen_model._pack_weights_packed(torch.from_numpy(q.astype(np.int8)), torch.from_numpy(s).to(torch.bfloat16),
+                                                     torch.from_numpy(z.astype(np.int8)), k, n, spec)
+            hm_model._write_tensor_raw(d / f"layer_0_{name}.packed.bin", packed)
+        qs = [weights[(0, nm)] for nm in ("q", "k", "v")]
+        cat = [np.concatenate([w[i] for w in qs], axis=1) for i in range(3)]
+        spec = qwen_model._resolve_layer_pad_packed_alignment(pad_default, {a: tuple(b) for a, b in pad_by.items()}, "qkv")
+        packed = qwen_model._pack_weights_packed(torch.from_numpy(cat[0].astype(np.int8)), torch.from_numpy(cat[1]).to(torch.bfloat16),
+                                                 torch.from_numpy(cat[2].astype(np.int8)), hidden, 384, spec)
+        hm_model._write_tensor_raw(d / "layer_0_qkv.packed.bin", packed)
+        manifest = {"format_version": 2, "model_name": "tiny-ffn", "use_packed_weights": True,
+                    "pad_packed_weights": list(pad_default), "pad_packed_weights_by_layer": pad_by, "heterogeneity": "gpu",
+                    "split_k_by_layer": {}, "num_hidden_layers": 1, "hidden_size": hidden, "intermediate_size": inter,
+                    "num_attention_heads": 1, "num_key_value_heads": 1, "head_dim": 128, "groupsize": 128,
+                    "qwen_fused_qkv_bins": True}
+        (d / "manifest.json").write_text(json.dumps(manifest, indent=2))
+        names = sorted(f.name for f in d.iterdir())
+        out["qwen_files"] = np.array(names)
+        for f in names:
+            out[f"qwen/{f}"] = np.frombuffer((d / f).read_bytes(), np.uint8)
     np.savez_compressed(os.path.join(HERE, "checkpoint.npz"), **out)
 
 
