@@ -1,7 +1,7 @@
 """Generate the golden fixtures in this folder from the reference's own code.
 
-Run in a container that holds the reference tree (default /root/reference, or
-$HETEROMEGA_REF) after ``make -C oracle ref``:
+Run where the reference tree is available (its location in $HETEROMEGA_REF, else the default
+below) after ``make -C oracle ref``:
 
     python tests/golden/make_golden.py
 
