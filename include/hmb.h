@@ -176,9 +176,12 @@ int hmb_selftest_bounded_wait(int64_t limit_ns, hmb_stream_t stream);
 /* Tensor-parallel boundary sum over NVLink peer memory (the counterpart of the per-layer partial sum:
  * heteromega::residual_add2, kernels/gpu/src/residual_add.cu:55-73; MergedFfn::add_out,
  * src/unified_llm_w4a16_hetero/merged_ffn.cpp:417). One communicator per rank of a P-rank group
- * (P <= 8, one GPU each): hmb_comm_create allocates this rank's receive slots and flag words and
- * writes its CUDA IPC handle (hmb_comm_handle_bytes bytes); after the handles of all ranks are
- * exchanged (rank order), hmb_comm_connect opens the peers'. hmb_allreduce_partials then replaces
+ * (P <= 8, one GPU each): hmb_comm_create allocates this rank's flag words, receive slots and the
+ * output region of hmb_allreduce_residual_norm (about 5 x max_bytes in all; max_bytes must be the same
+ * on every rank) and writes its CUDA IPC handle (hmb_comm_handle_bytes bytes); after the handles of
+ * all ranks are exchanged (rank order), hmb_comm_connect opens the peers'. The communicator's kernels
+ * keep 128 CTAs resident while they run and must not share the GPU with another kernel that waits
+ * on them. hmb_allreduce_partials then replaces
  * y (bf16, fp16 or fp32; elems * size a multiple of 16 bytes, at most max_bytes) on every rank by
  * the sum over the ranks: fp32 sums in rank order, one rounding, the same bits everywhere. Every
  * rank must make the same calls in the same order. Waits give up after spin_limit_ns (0: one
