@@ -50,7 +50,7 @@ SIGNATURES = {
     "hmb_comm_connect": (_int, [_vp, _vp]),
     "hmb_allreduce_partials": (_int, [_vp, _i64, _int, _vp, _vp, ctypes.c_uint64]),
     "hmb_comm_destroy": (_int, [_vp]),
-    "hmb_allreduce_residual_norm": (_int, [_vp, _vp, _vp, _i64, _i64, ctypes.c_float, _vp, _vp, ctypes.c_uint64]),
+    "hmb_allreduce_residual_norm": (_int, [_vp, _int, _vp, _vp, _i64, _i64, ctypes.c_float, _vp, _vp, ctypes.c_uint64]),
     "hmb_comm_out": (_int, [_vp, _vp, _vp]),
     "hmb_tp_ffn_layer": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp, _vp, _vp, ctypes.c_float, _i64, _vp, _sz, _vp,
                                 ctypes.c_uint64]),

@@ -75,7 +75,7 @@ struct ArArgs {
 
 struct BnArgs {
     Link l;
-    const uint16_t *y;  // this rank's partial [m, h]
+    const void *y;      // this rank's partial [m, h]: bf16, or fp32 (AT of the kernel)
     uint16_t *x;        // the residual [m, h]
     const uint16_t *w;  // norm weight [h], or null
     int64_t m;
@@ -284,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1) allreduce_kernel(const ArArgs a) 
 // The layer boundary. One-shot: every rank gets every partial and computes every row (the residual
 // stays whole on every rank). Two-shot: rank c receives the rows it owns from every rank, computes
 // them, keeps x for those rows, and stores the normed rows into every rank's output region.
-template <int V, int NW>
+template <int V, int NW, typename AT>
 __global__ void __launch_bounds__(kThreads, 1) boundary_kernel(const BnArgs a) {
     __shared__ unsigned s_epoch;
     __shared__ int s_ok;
@@ -295,9 +295,10 @@ __global__ void __launch_bounds__(kThreads, 1) boundary_kernel(const BnArgs a) {
     pdl_wait();  // y comes from the previous kernel
     const unsigned epoch = begin_call(l, &s_epoch, &s_ok);
     const int par = epoch & 1;
-    const int64_t row_bytes = 2 * static_cast<int64_t>(a.h);
-    const uint8_t *y = reinterpret_cast<const uint8_t *>(a.y);
-    const uint16_t *in[kMaxRanks];
+    const int64_t row_bytes = static_cast<int64_t>(sizeof(AT)) * a.h;  // a partial row, in y and in the slots
+    const uint8_t *y = static_cast<const uint8_t *>(a.y);
+    const AT *ya = static_cast<const AT *>(a.y);
+    const AT *in[kMaxRanks];
     uint16_t *out[kMaxRanks];
 
     // This rank's own partial: y, or (prefilled) its own slot like every other rank's.
@@ -310,10 +311,10 @@ __global__ void __launch_bounds__(kThreads, 1) boundary_kernel(const BnArgs a) {
         for (int64_t row = blockIdx.x; row < a.m; row += kCtas) {
 #pragma unroll
             for (int r = 0; r < NW; ++r)
-                in[r] = r == l.rank && own_y ? a.y + row * a.h
-                                             : reinterpret_cast<const uint16_t *>(slot(l, l.rank, 0, par, r) + row * row_bytes);
+                in[r] = r == l.rank && own_y ? ya + row * a.h
+                                             : reinterpret_cast<const AT *>(slot(l, l.rank, 0, par, r) + row * row_bytes);
             out[0] = reinterpret_cast<uint16_t *>(l.p.base[l.rank] + a.out_offset) + row * a.h;
-            boundary_row<V, NW>(in, a.x + row * a.h, true, a.w, a.h, a.eps, out, 1, red);
+            boundary_row<V, NW, AT>(in, a.x + row * a.h, true, a.w, a.h, a.eps, out, 1, red);
         }
         return;
     }
@@ -331,37 +332,42 @@ __global__ void __launch_bounds__(kThreads, 1) boundary_kernel(const BnArgs a) {
     for (int64_t row = r0 + blockIdx.x; row < r1; row += kCtas) {
 #pragma unroll
         for (int r = 0; r < NW; ++r) {
-            in[r] = r == l.rank && own_y ? a.y + row * a.h
-                                         : reinterpret_cast<const uint16_t *>(slot(l, l.rank, 0, par, r) + (row - r0) * row_bytes);
+            in[r] = r == l.rank && own_y ? ya + row * a.h
+                                         : reinterpret_cast<const AT *>(slot(l, l.rank, 0, par, r) + (row - r0) * row_bytes);
             out[r] = reinterpret_cast<uint16_t *>(l.p.base[r] + a.out_offset) + row * a.h;
         }
-        boundary_row<V, NW>(in, a.x + row * a.h, true, a.w, a.h, a.eps, out, NW, red);
+        boundary_row<V, NW, AT>(in, a.x + row * a.h, true, a.w, a.h, a.eps, out, NW, red);
     }
     // The kernel ends only when every rank's rows have arrived in this rank's output region.
     raise_flags(l, 1, par, epoch);
     wait_all_ctas(l, 1, par, epoch, &s_ok);
 }
 
-template <int V>
+template <int V, typename AT>
 cudaError_t launch_boundary_v(int world, cudaStream_t s, const BnArgs &a) {
     const dim3 g(kCtas), b(kThreads);
     switch (world) {
-        case 1: return launch_pdl(boundary_kernel<V, 1>, g, b, 0, s, a);
-        case 2: return launch_pdl(boundary_kernel<V, 2>, g, b, 0, s, a);
-        case 3: return launch_pdl(boundary_kernel<V, 3>, g, b, 0, s, a);
-        case 4: return launch_pdl(boundary_kernel<V, 4>, g, b, 0, s, a);
-        case 5: return launch_pdl(boundary_kernel<V, 5>, g, b, 0, s, a);
-        case 6: return launch_pdl(boundary_kernel<V, 6>, g, b, 0, s, a);
-        case 7: return launch_pdl(boundary_kernel<V, 7>, g, b, 0, s, a);
-        default: return launch_pdl(boundary_kernel<V, 8>, g, b, 0, s, a);
+        case 1: return launch_pdl(boundary_kernel<V, 1, AT>, g, b, 0, s, a);
+        case 2: return launch_pdl(boundary_kernel<V, 2, AT>, g, b, 0, s, a);
+        case 3: return launch_pdl(boundary_kernel<V, 3, AT>, g, b, 0, s, a);
+        case 4: return launch_pdl(boundary_kernel<V, 4, AT>, g, b, 0, s, a);
+        case 5: return launch_pdl(boundary_kernel<V, 5, AT>, g, b, 0, s, a);
+        case 6: return launch_pdl(boundary_kernel<V, 6, AT>, g, b, 0, s, a);
+        case 7: return launch_pdl(boundary_kernel<V, 7, AT>, g, b, 0, s, a);
+        default: return launch_pdl(boundary_kernel<V, 8, AT>, g, b, 0, s, a);
     }
 }
 
-cudaError_t launch_boundary(int v, int world, cudaStream_t s, const BnArgs &a) {
-    if (v == 1) return launch_boundary_v<1>(world, s, a);
-    if (v == 2) return launch_boundary_v<2>(world, s, a);
-    if (v == 4) return launch_boundary_v<4>(world, s, a);
-    return launch_boundary_v<8>(world, s, a);
+template <typename AT>
+cudaError_t launch_boundary_t(int v, int world, cudaStream_t s, const BnArgs &a) {
+    if (v == 1) return launch_boundary_v<1, AT>(world, s, a);
+    if (v == 2) return launch_boundary_v<2, AT>(world, s, a);
+    if (v == 4) return launch_boundary_v<4, AT>(world, s, a);
+    return launch_boundary_v<8, AT>(world, s, a);
+}
+
+cudaError_t launch_boundary(int v, int world, bool f32, cudaStream_t s, const BnArgs &a) {
+    return f32 ? launch_boundary_t<float>(v, world, s, a) : launch_boundary_t<uint16_t>(v, world, s, a);
 }
 
 }  // namespace
@@ -398,6 +404,8 @@ Link make_link(const hmb_comm *c, uint64_t spin_limit_ns, int *status) {
 
 namespace hmb {
 
+int comm_world(const hmb_comm *c) { return c ? c->world : 0; }
+
 int comm_scatter_target(const hmb_comm *c, int64_t m, int64_t h, ScatterTarget *t) {
     if (!c || !t || m <= 0 || h <= 0 || h % 8) return HMB_ERR_ARG;
     if (!c->connected) return HMB_ERR_ARG;
@@ -418,22 +426,27 @@ int comm_scatter_target(const hmb_comm *c, int64_t m, int64_t h, ScatterTarget *
     return HMB_OK;
 }
 
-int comm_boundary(hmb_comm *c, const void *y, void *x, const void *weight, int64_t m, int64_t h, float eps, bool prefilled,
-                  cudaStream_t s, uint64_t spin_limit_ns) {
+int comm_boundary(hmb_comm *c, const void *y, int y_dtype, void *x, const void *weight, int64_t m, int64_t h, float eps,
+                  bool prefilled, cudaStream_t s, uint64_t spin_limit_ns) {
     if (!x || !c || m <= 0 || h <= 0 || h % 8 || h > kRowMaxH || !(eps >= 0.0f)) return HMB_ERR_ARG;
     if (!c->connected || (!y && !prefilled)) return HMB_ERR_ARG;
+    if (y_dtype != HMB_BF16 && y_dtype != HMB_FP32) return HMB_ERR_ARG;
+    if (prefilled && y_dtype != HMB_BF16) return HMB_ERR_ARG;  // the scattering GEMM writes bf16
     if ((y && !aligned(y, 16)) || !aligned(x, 16) || (weight && !aligned(weight, 16))) return HMB_ERR_ALIGN;
-    const int64_t bytes = m * h * 2;
+    // One-shot or two-shot by the bf16 size of the message, whatever the partials' type, so the rows
+    // a rank keeps (hmb_comm_rows) do not depend on it; a one-shot slot holds fp32 partials too.
+    const int64_t bytes = m * h * 2, esz = y_dtype == HMB_FP32 ? 4 : 2;
     if (static_cast<size_t>(bytes) > c->max_bytes) return HMB_ERR_WORKSPACE;
     void *out = c->mine + c->out_offset;
     const bool two_shot = bytes > kOneShotBytes && c->world > 1;
-    if (two_shot && static_cast<size_t>((comm_share_row(m, c->world, 1) + 1) * 2 * h) > c->slot_bytes) return HMB_ERR_WORKSPACE;
-    if (c->world == 1 && !prefilled) return residual_norm_launch(x, h, y, h, nullptr, 0, weight, out, h, m, h, eps, s);
+    const int64_t slot_need = two_shot ? (comm_share_row(m, c->world, 1) + 1) * esz * h : m * h * esz;
+    if (static_cast<size_t>(slot_need) > c->slot_bytes) return HMB_ERR_WORKSPACE;
+    if (c->world == 1 && !prefilled && y_dtype == HMB_BF16) return residual_norm_launch(x, h, y, h, nullptr, 0, weight, out, h, m, h, eps, s);
     int *status = device_status_word();
     if (!status) return HMB_ERR_CUDA;
     BnArgs a{};
     a.l = make_link(c, spin_limit_ns, status);
-    a.y = static_cast<const uint16_t *>(y);
+    a.y = y;
     a.x = static_cast<uint16_t *>(x);
     a.w = static_cast<const uint16_t *>(weight);
     a.m = m;
@@ -442,7 +455,7 @@ int comm_boundary(hmb_comm *c, const void *y, void *x, const void *weight, int64
     a.two_shot = two_shot;
     a.prefilled = prefilled;
     a.out_offset = static_cast<int64_t>(c->out_offset);
-    const cudaError_t e = launch_boundary(row_vectors(h), c->world, s, a);
+    const cudaError_t e = launch_boundary(row_vectors(h), c->world, y_dtype == HMB_FP32, s, a);
     if (e != cudaSuccess) {
         set_cuda_error(e);
         return HMB_ERR_CUDA;
@@ -463,9 +476,10 @@ int hmb_comm_create(int rank, int world, size_t max_bytes, hmb_comm **out, void 
     c->world = world;
     cudaGetDevice(&c->device);
     c->max_bytes = (max_bytes + 255) / 256 * 256;
-    // A one-shot slot holds a whole message (<= kOneShotBytes), a two-shot slot one chunk of it (for
-    // the boundary, one rank's rows: at most one row more than 1/P of the message).
-    c->slot_bytes = std::max<size_t>(kOneShotBytes, ((c->max_bytes + world - 1) / world + kRowSlack + 255) / 256 * 256);
+    // A one-shot slot holds a whole message (<= kOneShotBytes, twice that for the boundary's fp32
+    // partials), a two-shot slot one chunk of it (for the boundary, one rank's rows: at most one row
+    // more than 1/P of the message).
+    c->slot_bytes = std::max<size_t>(2 * kOneShotBytes, ((c->max_bytes + world - 1) / world + kRowSlack + 255) / 256 * 256);
     c->out_offset = kFlagBytes + 2 * 2 * static_cast<size_t>(world) * c->slot_bytes;
     const size_t bytes = c->out_offset + c->max_bytes;
     cudaError_t e = cudaMalloc(&c->mine, bytes);
@@ -552,10 +566,10 @@ int hmb_comm_rows(const hmb_comm *c, int64_t m, int64_t h, int64_t *begin, int64
     return HMB_OK;
 }
 
-int hmb_allreduce_residual_norm(const void *y, void *x, const void *weight, int64_t m, int64_t h, float eps, hmb_comm *c,
+int hmb_allreduce_residual_norm(const void *y, int y_dtype, void *x, const void *weight, int64_t m, int64_t h, float eps, hmb_comm *c,
                                 hmb_stream_t stream, uint64_t spin_limit_ns) {
     if (!y) return HMB_ERR_ARG;
-    return comm_boundary(c, y, x, weight, m, h, eps, false, static_cast<cudaStream_t>(stream), spin_limit_ns);
+    return comm_boundary(c, y, y_dtype, x, weight, m, h, eps, false, static_cast<cudaStream_t>(stream), spin_limit_ns);
 }
 
 int hmb_comm_destroy(hmb_comm *c) {

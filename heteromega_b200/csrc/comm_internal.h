@@ -46,12 +46,15 @@ __device__ __forceinline__ uint16_t *scatter_row(const ScatterTarget &t, int par
 __device__ __forceinline__ int scatter_parity(const ScatterTarget &t) { return (*reinterpret_cast<const volatile unsigned *>(t.epochs) + 1) & 1; }
 #endif
 
+// Ranks in the communicator's group (0 for null).
+int comm_world(const hmb_comm *c);
+
 // The scatter target of an m x h boundary on this communicator (HMB_ERR_WORKSPACE if it does not fit).
 int comm_scatter_target(const hmb_comm *c, int64_t m, int64_t h, ScatterTarget *t);
 
 // hmb_allreduce_residual_norm; with `prefilled` the partials are already in the slots (written by
-// a scatter to comm_scatter_target) and y is not read.
-int comm_boundary(hmb_comm *c, const void *y, void *x, const void *weight, int64_t m, int64_t h, float eps, bool prefilled,
-                  cudaStream_t stream, uint64_t spin_limit_ns);
+// a scatter to comm_scatter_target, bf16) and y is not read.
+int comm_boundary(hmb_comm *c, const void *y, int y_dtype, void *x, const void *weight, int64_t m, int64_t h, float eps,
+                  bool prefilled, cudaStream_t stream, uint64_t spin_limit_ns);
 
 }  // namespace hmb

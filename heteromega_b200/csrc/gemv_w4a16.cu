@@ -770,7 +770,7 @@ int hmb_w4a16_ffn(const uint8_t *gate_up, const uint8_t *down, int64_t h, int64_
 
 size_t hmb_tp_ffn_layer_workspace(int64_t m, int64_t h, int64_t n) {
     const size_t ffn = hmb_w4a16_ffn_workspace(m, h, n);
-    return ffn ? ffn + round256(static_cast<size_t>(m) * h * 2) : 0;
+    return ffn ? ffn + round256(static_cast<size_t>(m) * h * 4) : 0;
 }
 
 int hmb_tp_ffn_layer(hmb_comm *comm, const uint8_t *gate_up, const uint8_t *down, int64_t h, int64_t n, int64_t stored, int layout,
@@ -783,7 +783,7 @@ int hmb_tp_ffn_layer(hmb_comm *comm, const uint8_t *gate_up, const uint8_t *down
     if (!aligned(workspace, 256)) return HMB_ERR_ALIGN;
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     uint8_t *ws = static_cast<uint8_t *>(workspace);
-    void *y = ws + ffn_bytes;  // this rank's partial, when it is not scattered
+    void *y = ws + ffn_bytes;  // this rank's partial, when it is not scattered (fp32 on two or more ranks)
 
     // Prefill on two or more ranks: gate/up GEMM with SwiGLU, then the down GEMM storing its partial
     // rows over NVLink into the receive slots of the boundary, which then only sums and normalises.
@@ -806,12 +806,15 @@ int hmb_tp_ffn_layer(hmb_comm *comm, const uint8_t *gate_up, const uint8_t *down
         rc = gemm_run(down, stored, h, act_p, n, HMB_BF16, nullptr, h, HMB_BF16, m, n, h, 0, HMB_EPI_STORE, 0, scratch, scratch_bytes,
                       dn_split_cnt, s, &t);
         if (rc != HMB_OK) return rc;
-        return comm_boundary(comm, nullptr, resid, norm_weight, m, h, eps, true, s, spin_limit_ns);
+        return comm_boundary(comm, nullptr, HMB_BF16, resid, norm_weight, m, h, eps, true, s, spin_limit_ns);
     }
-    // Decode (and a group of one): the FFN into y, then the boundary with its own exchange.
-    int rc = hmb_w4a16_ffn(gate_up, down, h, n, stored, layout, x, h, HMB_BF16, y, h, HMB_BF16, m, workspace, ffn_bytes, stream);
+    // Decode (and a group of one): the FFN into y, then the boundary with its own exchange. Across
+    // ranks the partials stay fp32 (unrounded sums): the messages are small, and P rounded partials
+    // would add P roundings to every layer's sum.
+    const int y_dtype = comm_world(comm) > 1 ? HMB_FP32 : HMB_BF16;
+    int rc = hmb_w4a16_ffn(gate_up, down, h, n, stored, layout, x, h, HMB_BF16, y, h, y_dtype, m, workspace, ffn_bytes, stream);
     if (rc != HMB_OK) return rc;
-    return comm_boundary(comm, y, resid, norm_weight, m, h, eps, false, s, spin_limit_ns);
+    return comm_boundary(comm, y, y_dtype, resid, norm_weight, m, h, eps, false, s, spin_limit_ns);
 }
 
 }  // extern "C"

@@ -45,33 +45,63 @@ __device__ __forceinline__ uint4 pack8(const float *f) {
     return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// 8 addend values as loaded: bf16 (one 16-byte word) or fp32 (two).
+template <typename AT>
+struct Addend8;
+template <>
+struct Addend8<uint16_t> {
+    static constexpr int kWords = 1;
+    uint4 w;
+    __device__ __forceinline__ void load(const uint16_t *p) { w = *reinterpret_cast<const uint4 *>(p); }
+    __device__ __forceinline__ void add_to(float *acc) const {
+        float f[8];
+        unpack8(w, f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] += f[e];
+    }
+};
+template <>
+struct Addend8<float> {
+    static constexpr int kWords = 2;
+    float4 a, b;
+    __device__ __forceinline__ void load(const float *p) {
+        a = *reinterpret_cast<const float4 *>(p);
+        b = *reinterpret_cast<const float4 *>(p + 4);
+    }
+    __device__ __forceinline__ void add_to(float *acc) const {
+        acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+        acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+    }
+};
+
 // Vectors of 8 values per thread for rows of h values: V = 1, 2, 4 or 8 (h <= 2048 V).
 __host__ __device__ constexpr int row_vectors(int64_t h) { return h <= 2048 ? 1 : h <= 4096 ? 2 : h <= 8192 ? 4 : 8; }
 
-// in[0..NIN): addend rows (bf16, h values). x: the residual row, overwritten with x_new when NIN > 0
-// and write_x. out[0..n_out): rows that all receive the result. w: the norm weight row or null.
-// h % 8 == 0, h <= V * 2048; every pointer 16-byte aligned. All threads of the CTA must call.
-// The loads of x and of every addend are issued before the sums (no load waits for an add), so a
-// row costs about one memory latency, not one per addend.
-template <int V, int NIN>
-__device__ __forceinline__ void boundary_row(const uint16_t *const *in, uint16_t *x, bool write_x, const uint16_t *w, int h,
-                                             float eps, uint16_t *const *out, int n_out, float *red) {
+// in[0..NIN): addend rows (h values of AT: bf16 bits or fp32). x: the residual row, overwritten with
+// x_new when NIN > 0 and write_x. out[0..n_out): rows that all receive the result. w: the norm weight
+// row or null. h % 8 == 0, h <= V * 2048; every pointer 16-byte aligned. All threads of the CTA must
+// call. The loads of x and of every addend are issued before the sums (no load waits for an add), so
+// a row costs about one memory latency, not one per addend.
+template <int V, int NIN, typename AT = uint16_t>
+__device__ __forceinline__ void boundary_row(const AT *const *in, uint16_t *x, bool write_x, const uint16_t *w, int h, float eps,
+                                             uint16_t *const *out, int n_out, float *red) {
     const int nv = h >> 3;
     // Vectors in groups of G: every load of a group (x and the addends) is in flight at once, and a
     // group's loads stay within the registers.
-    constexpr int G = V * (NIN + 1) <= 40 ? V : (40 / (NIN + 1) >= 1 ? 40 / (NIN + 1) : 1);
+    constexpr int kCost = 1 + NIN * Addend8<AT>::kWords;
+    constexpr int G = V * kCost <= 40 ? V : (40 / kCost >= 1 ? 40 / kCost : 1);
     uint4 xv[V];
     float ss = 0.0f;
 #pragma unroll
     for (int i0 = 0; i0 < V; i0 += G) {
-        uint4 pv[NIN > 0 ? NIN : 1][G];
+        Addend8<AT> pv[NIN > 0 ? NIN : 1][G];
 #pragma unroll
         for (int j = 0; j < G && i0 + j < V; ++j) {
             const int v = (i0 + j) * kRowThreads + threadIdx.x;
             if (v < nv) {
                 xv[i0 + j] = *reinterpret_cast<const uint4 *>(x + 8 * v);
 #pragma unroll
-                for (int r = 0; r < NIN; ++r) pv[r][j] = *reinterpret_cast<const uint4 *>(in[r] + 8 * v);
+                for (int r = 0; r < NIN; ++r) pv[r][j].load(in[r] + 8 * v);
             }
         }
 #pragma unroll
@@ -82,12 +112,7 @@ __device__ __forceinline__ void boundary_row(const uint16_t *const *in, uint16_t
                     float acc[8];
                     unpack8(xv[i0 + j], acc);
 #pragma unroll
-                    for (int r = 0; r < NIN; ++r) {
-                        float p[8];
-                        unpack8(pv[r][j], p);
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) acc[e] += p[e];
-                    }
+                    for (int r = 0; r < NIN; ++r) pv[r][j].add_to(acc);
                     xv[i0 + j] = pack8(acc);
                     if (write_x) *reinterpret_cast<uint4 *>(x + 8 * v) = xv[i0 + j];
                 }

@@ -72,15 +72,18 @@ class PeerComm:
     def boundary(self, y, x, weight=None, eps=1e-5, spin_limit_ns=0):
         """The layer boundary (hmb_allreduce_residual_norm): x[rows] += the rank sum of y, then
         RMSNorm(x) * weight (x itself without weight) into the output region, whose [m, h] view it
-        returns. y and x: contiguous bf16 [m, h] on this rank's GPU; weight bf16 [h] or None."""
+        returns. y: contiguous bf16 or fp32 [m, h] partials, x: contiguous bf16 [m, h], both on this
+        rank's GPU; weight bf16 [h] or None."""
         m, h = x.shape
-        for name, t in (("y", y), ("x", x)):
-            if t.dtype != torch.bfloat16 or not t.is_contiguous() or tuple(t.shape) != (m, h) or t.device != self.device:
-                raise ValueError(f"PeerComm.boundary: {name} must be contiguous bf16 [m, h] on the communicator's device")
+        for name, t, dtypes in (("y", y, (torch.bfloat16, torch.float32)), ("x", x, (torch.bfloat16,))):
+            if t.dtype not in dtypes or not t.is_contiguous() or tuple(t.shape) != (m, h) or t.device != self.device:
+                raise ValueError(f"PeerComm.boundary: {name} must be contiguous {'/'.join(str(d) for d in dtypes)} [m, h] "
+                                 "on the communicator's device")
         if weight is not None and (weight.dtype != torch.bfloat16 or weight.numel() != h or not weight.is_contiguous()):
             raise ValueError("PeerComm.boundary: weight must be contiguous bf16 [h]")
         out = self.out(m, h)
-        check(lib().hmb_allreduce_residual_norm(y.data_ptr(), x.data_ptr(), weight.data_ptr() if weight is not None else None,
+        code = _lib.HMB_FP32 if y.dtype == torch.float32 else _lib.HMB_BF16
+        check(lib().hmb_allreduce_residual_norm(y.data_ptr(), code, x.data_ptr(), weight.data_ptr() if weight is not None else None,
                                                 m, h, float(eps), self._ptr, torch.cuda.current_stream(self.device).cuda_stream,
                                                 spin_limit_ns), "hmb_allreduce_residual_norm")
         return out

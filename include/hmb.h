@@ -200,7 +200,9 @@ int hmb_comm_destroy(hmb_comm *comm);
  *   x   = bf16(((x + y_0) + y_1) + ... + y_{P-1})            y_r = rank r's partial, fp32, one rounding
  *   out = bf16((x * rsqrt(sum(x^2) / h + eps)) * weight)     weight null: out = x
  * and `out`, the communicator's output region (hmb_comm_out), holds all m rows on every rank when the
- * call completes, the same bits everywhere; it is the next layer's input. y, x: bf16 [m, h] rows, ld = h;
+ * call completes, the same bits everywhere; it is the next layer's input. y: [m, h] partials of
+ * y_dtype (HMB_BF16 as the reference's GPU partial, or HMB_FP32 for unrounded sums); x: bf16 [m, h];
+ * both with ld = h;
  * weight bf16 [h]; h a multiple of 8, at most 16384; m * h * 2 at most the communicator's max_bytes
  * (which must be the same on every rank). Messages up to 512 KB run one-shot: every rank owns every
  * row, so x stays whole on every rank. Larger ones reduce-scatter by rows: rank c owns rows
@@ -208,8 +210,8 @@ int hmb_comm_destroy(hmb_comm *comm);
  * rows into every rank's output region; the other rows of x are neither read nor written. Every rank
  * must make the same calls in the same order; waits give up after spin_limit_ns (0: one second) with
  * HMB_ERR_TIMEOUT in the device status word. A group of one runs hmb_residual_norm into the output. */
-int hmb_allreduce_residual_norm(const void *y, void *x, const void *weight, int64_t m, int64_t h, float eps, hmb_comm *comm,
-                                hmb_stream_t stream, uint64_t spin_limit_ns);
+int hmb_allreduce_residual_norm(const void *y, int y_dtype, void *x, const void *weight, int64_t m, int64_t h, float eps,
+                                hmb_comm *comm, hmb_stream_t stream, uint64_t spin_limit_ns);
 /* One tensor-parallel FFN layer with its boundary, end to end on this rank: this rank's channel slice
  * of the layer (as hmb_w4a16_ffn: gate_up, down, h, n, stored, layout) for x[m, h] (bf16, ld = h;
  * normally the output region holding the previous boundary's result), then the boundary of
@@ -217,7 +219,8 @@ int hmb_allreduce_residual_norm(const void *y, void *x, const void *weight, int6
  * For m > 16 on two or more ranks the down GEMM stores its partial rows over NVLink straight into
  * the receive slots the boundary reads (the owner's rows, or every rank's for one-shot sizes), so
  * the reduce-scatter overlaps the GEMM tile by tile and the boundary only sums, normalises and
- * gathers; otherwise the partial goes to the workspace and the boundary exchanges it. workspace:
+ * gathers; otherwise (decode) the partial goes to the workspace, in fp32 on two or more ranks, and the
+ * boundary exchanges it. workspace:
  * hmb_tp_ffn_layer_workspace(m, h, n) bytes, 256-byte aligned, zero-filled once before the first call.
  * Replaces, per layer, GpuFfnModel::forward plus the boundary of the model loop
  * (kernels/gpu/src/gpu_ffn.cpp:142-156; src/unified_llm_w4a16_hetero/unified_llm_w4a16.cpp:2533-2540,

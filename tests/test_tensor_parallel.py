@@ -208,19 +208,21 @@ def _gpu_boundary_rank(rank, world, port, out_path):
         res = {}
         for rnd in range(2):  # the second round reuses the double-buffered slots with advanced epochs
             for m, h in BOUNDARY_CASES:
-                for weighted in (True, False):
-                    tag = f"{m}_{h}_{int(weighted)}_{rnd}"
+                for weighted, dt in ((True, "bf16"), (False, "bf16"), (True, "f32")):
+                    tag = f"{m}_{h}_{int(weighted)}_{rnd}_{dt}"
                     gx = torch.Generator(device=dev).manual_seed(m * 31 + h + rnd)  # the same on every rank
                     x = torch.randn(m, h, device=dev, generator=gx).to(torch.bfloat16)
                     w = (torch.randn(h, device=dev, generator=gx) * 0.2 + 1.0).to(torch.bfloat16)
                     gy = torch.Generator(device=dev).manual_seed(m * 31 + h + rnd + 1000 * (rank + 1))
-                    y = (torch.randn(m, h, device=dev, generator=gy) * 3).to(torch.bfloat16)
+                    y = torch.randn(m, h, device=dev, generator=gy) * 3
+                    y = y.to(torch.bfloat16) if dt == "bf16" else y
                     x0 = x.clone()
                     out = comm.boundary(y, x, w if weighted else None, 1e-5)
                     torch.cuda.synchronize()
                     b, e = comm.rows(m, h)
                     bits = lambda t: t.cpu().view(torch.int16).numpy()  # noqa: E731
-                    res[f"x0_{tag}"], res[f"y_{tag}"], res[f"w_{tag}"] = bits(x0), bits(y), bits(w)
+                    res[f"x0_{tag}"], res[f"w_{tag}"] = bits(x0), bits(w)
+                    res[f"y_{tag}"] = bits(y) if dt == "bf16" else y.cpu().numpy()
                     res[f"out_{tag}"], res[f"x_{tag}"] = bits(out), bits(x[b:e])
                     res[f"rows_{tag}"] = np.array([b, e])
         from heteromega_b200.torch_ops import device_status
@@ -238,9 +240,10 @@ def _gpu_boundary_rank(rank, world, port, out_path):
 @pytest.mark.gpu
 def test_two_gpu_boundary_matches_oracle(tmp_path, oracle):
     """The fused tensor-parallel boundary (hmb_allreduce_residual_norm) on 2 GPUs, one-shot (up to 512 KB)
-    and two-shot (rows split between the ranks) sizes, with and without a norm weight, against the
-    oracle's boundary with the two rank partials as its addends in rank order: the kept rows of x bit
-    for bit, the output on both ranks the same bits and within one bf16 rounding of the oracle."""
+    and two-shot (rows split between the ranks) sizes, with and without a norm weight, with bf16 and
+    fp32 partials, against the oracle's boundary with the two rank partials as its addends in rank
+    order: the kept rows of x bit for bit, the output on both ranks the same bits and within one bf16
+    rounding of the oracle."""
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     out = str(tmp_path / "bn")
@@ -252,11 +255,18 @@ def test_two_gpu_boundary_matches_oracle(tmp_path, oracle):
     u16 = lambda a: a.view(np.uint16)  # noqa: E731
     for rnd in range(2):
         for m, h in BOUNDARY_CASES:
-            for weighted in (1, 0):
-                tag = f"{m}_{h}_{weighted}_{rnd}"
+            for weighted, dt in ((1, "bf16"), (0, "bf16"), (1, "f32")):
+                tag = f"{m}_{h}_{weighted}_{rnd}_{dt}"
                 assert np.array_equal(r[0][f"out_{tag}"], r[1][f"out_{tag}"]), f"ranks disagree {tag}"
-                ref_x, ref_n = oracle.residual_norm(u16(r[0][f"x0_{tag}"]), [u16(r[0][f"y_{tag}"]), u16(r[1][f"y_{tag}"])],
-                                                    u16(r[0][f"w_{tag}"]) if weighted else None, 1e-5)
+                if dt == "bf16":
+                    ref_x, ref_n = oracle.residual_norm(u16(r[0][f"x0_{tag}"]), [u16(r[0][f"y_{tag}"]), u16(r[1][f"y_{tag}"])],
+                                                        u16(r[0][f"w_{tag}"]) if weighted else None, 1e-5)
+                else:
+                    # fp32 partials: x + y_0 + y_1 in fp32, left to right, one rounding; then the norm
+                    acc = oracle.bf16_to_f32(u16(r[0][f"x0_{tag}"])).astype(np.float32)
+                    for rank in range(2):
+                        acc = (acc + r[rank][f"y_{tag}"]).astype(np.float32)
+                    ref_x, ref_n = oracle.residual_norm(oracle.bf16_bits(acc), [], u16(r[0][f"w_{tag}"]), 1e-5)
                 covered = np.zeros(m, bool)
                 for rank in range(2):
                     b, e = r[rank][f"rows_{tag}"]
