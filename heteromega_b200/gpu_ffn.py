@@ -18,6 +18,7 @@ Differences from the reference, all deliberate:
 """
 import dataclasses
 import enum
+import os
 import threading
 
 import numpy as np
@@ -394,6 +395,21 @@ class GpuFfnModel:
             if not (0 < s <= inter and s % kTileK == 0):
                 raise ValueError(f"GpuFfnModel::set_split: channels must be a multiple of 128 in (0, {inter}], got {s}")
         self._s_prefill, self._s_decode = s_prefill, s_decode
+
+    def split_from_env(self, environ=None):
+        """Applies HETEROMEGA_GPU_FFN_SPLIT="<s_prefill>,<s_decode>" when it is set (the model setup of
+        src/unified_llm_w4a16_hetero/unified_llm_w4a16.cpp:2377-2382); returns whether it was."""
+        env = os.environ if environ is None else environ
+        value = env.get("HETEROMEGA_GPU_FFN_SPLIT")
+        if value is None:
+            return False
+        parts = value.split(",")
+        try:
+            s_prefill, s_decode = (int(p) for p in parts)
+        except ValueError:
+            raise ValueError(f"HETEROMEGA_GPU_FFN_SPLIT must be <s_prefill>,<s_decode>, got {value}") from None
+        self.set_split(s_prefill, s_decode)
+        return True
 
     def layers(self):
         return len(self._layers)

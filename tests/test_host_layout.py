@@ -136,3 +136,22 @@ def test_gpu_ops_refuse_cpu_tensors():
     p = torch.zeros(4352, dtype=torch.uint8)
     with pytest.raises((ValueError, NotImplementedError, RuntimeError)):
         H.gemv_w4a16(y, x, p, 128, 64, 128, 64)
+
+
+def test_gpu_ffn_split_from_env():
+    """HETEROMEGA_GPU_FFN_SPLIT=<s_prefill>,<s_decode> as the reference's model setup reads it
+    (unified_llm_w4a16.cpp:2377-2382): both channel counts multiples of 128 within the layer."""
+    from heteromega_b200.weights import synthetic_layer
+
+    layer = synthetic_layer(256, 512, layer=0)
+    g, u, d = (H.pack_w4a16(q, s, z) for q, s, z in ((layer.gate_q, layer.gate_s, layer.gate_z),
+                                                     (layer.up_q, layer.up_s, layer.up_z),
+                                                     (layer.down_q, layer.down_s, layer.down_z)))
+    model = H.GpuFfnModel()
+    model.add_layer(g, u, d, 256, 512)
+    assert not model.split_from_env({})
+    assert model.split_from_env({"HETEROMEGA_GPU_FFN_SPLIT": "384,128"})
+    assert model.channels(7) == 384 and model.channels(1) == 128
+    for bad in ("384", "384,100", "a,b", "1024,128"):
+        with pytest.raises(ValueError):
+            model.split_from_env({"HETEROMEGA_GPU_FFN_SPLIT": bad})
