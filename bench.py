@@ -102,6 +102,21 @@ def peaks():
         return dict(FALLBACK_PEAKS), "fallback"
 
 
+def l2_flushed(wl, world):
+    """Whether a step's weights (this rank's share) fit in L2, so that L2 is flushed between steps."""
+    per_rank = wl["layers"] * 3 * wl["hidden"] * -(-wl["inter"] // world) * BYTES_PER_WEIGHT
+    return per_rank < 2 * L2_BYTES
+
+
+def config_of(wl, world, use_graph):
+    """The `config` object of the JSON line, the same for both arms of one workload."""
+    return {"workload": f"{wl['name']}: {wl['model']} x{wl['layers']} layers, M={wl['m']}", "hidden": wl["hidden"],
+            "intermediate": wl["inter"], "layers": wl["layers"], "m": wl["m"],
+            "parallelism": f"tp{world}" if world > 1 else "single",
+            "l2": "flushed between steps (2x L2 buffer written, then read)" if l2_flushed(wl, world) else "weights larger than L2",
+            "graph": use_graph}
+
+
 def layer_bytes(h, n, m):
     """Algorithmic HBM bytes of one FFN layer (all of its n channels): packed weights once, x in, y out."""
     return 3 * h * n * BYTES_PER_WEIGHT + 2 * m * h * 2
@@ -214,6 +229,7 @@ def run_hmb(args):
     tp = TensorParallelFfn(h, inter, rank=rank, world=world) if world > 1 else None
     layers, norms = [], []
     gen = torch.Generator(device=dev)
+    raw0 = None  # layer 0 unsliced (rank 0), for the parity check after the timed region
     for l in range(L):
         gen.manual_seed(1000 + l)
         g = synthetic_packed_device(h, inter, dev, gen)
@@ -223,6 +239,8 @@ def run_hmb(args):
             tp.add_layer(g, u, d)
         else:
             layers.append(H.slice_packed_ffn(g, u, d, h, inter, 0, inter, H.GateUpLayout.kInterleaved))
+        if l == 0 and rank == 0:
+            raw0 = (g, u, d)
         del g, u, d
         gen.manual_seed(2000 + l)
         norms.append((torch.randn(h, device=dev, generator=gen) * 0.2 + 1.0).to(torch.bfloat16))
@@ -236,8 +254,7 @@ def run_hmb(args):
     # reads RMSNorm of the running residual.
     gen.manual_seed(7)
     h0 = torch.randn(m, h, device=dev, generator=gen).to(torch.bfloat16)
-    weights_local = sum(w.gate_up.numel() + w.down.numel() for w in stack.layers)
-    flush = L2Flush(dev) if weights_local < 2 * L2_BYTES else None
+    flush = L2Flush(dev) if l2_flushed(wl, world) else None
 
     use_graph = not args.no_graph
     if use_graph:
@@ -290,6 +307,9 @@ def run_hmb(args):
     # End to end through the public API with host buffers (H2D of the step's inputs, D2H of its outputs).
     e2e = end_to_end(stack, h0, m, args, flush, barrier, world, dev)
     trace("e2e done")
+    # Parity of the timed code path: layer 0 and its boundary at the full M, sampled rows checked.
+    parity = parity_layer0(stack, raw0, h0, wl, tp, dev, rank)
+    trace("parity done")
 
     pk, pk_kind = peaks()
     from heteromega_b200.torch_ops import GEMV_MAX_ROWS
@@ -316,16 +336,14 @@ def run_hmb(args):
         "metric": "ffn_tokens_per_s", "value": round(tokens_per_s, 2), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded W4A16 group-128 weights, RMSNorm weights 1+0.2N(0,1), N(0,1) bf16 input)",
-        "config": {"workload": f"{wl['name']}: {wl['model']} x{L} layers, M={m}", "hidden": h, "intermediate": inter,
-                   "layers": L, "m": m, "parallelism": f"tp{world}" if world > 1 else "single",
-                   "l2": "flushed between steps (2x L2 buffer written, then read)" if flush is not None else "weights larger than L2",
-                   "graph": use_graph},
+        "config": config_of(wl, world, use_graph),
         "decode_hbm_gbs" if decode else "prefill_tflops":
             round(stack_bytes / (step_ms * 1e-3) / 1e9, 1) if decode else round(stack_flops / (step_ms * 1e-3) / 1e12, 1),
         "roofline": roof,
         "clocks": clocks.summary(),
         "e2e": e2e,
         "gpu_launches": stack.kernels_per_step() * args.steps,
+        "parity": parity,
     }
     if rank == 0 and world == 1:
         line["cpu_baseline"] = cpu_baseline(wl, m, args.cpu_sample_s)
@@ -341,6 +359,90 @@ def run_hmb(args):
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def parity_layer0(stack, raw0, h0, wl, tp, dev, rank, n_rows=64, eps=1e-5):
+    """Layer 0 and its boundary at the benchmark's full M through the same calls the timed step makes
+    (the first boundary, then hmb_w4a16_ffn and the boundary on one GPU, or hmb_tp_ffn_layer across the
+    ranks), checked on sampled rows (one per 256-row block up to n_rows, both CTA halves) against a torch
+    fp32 restatement of the reference's definition: weights dequantised exactly by hmb_w4a16_dequant (bit
+    for bit the oracle's (q - z) * s, pinned in tests/), gate and up as fp32 matmuls rounded to bf16,
+    SiLU(g) * u rounded once, down as an fp32 matmul; then h + y rounded once and RMSNorm * g. Every rank
+    runs the product path; rank 0 compares. Returns the `parity` object of the JSON line."""
+    import torch
+
+    from heteromega_b200.torch_ops import ops
+
+    m, h, inter, L = h0.shape[0], wl["hidden"], wl["inter"], wl["layers"]
+    g0, g1 = stack.norms[0], (stack.norms[1] if L > 1 else None)
+    hh = h0.clone()
+    if tp is not None and tp.comm is not None:
+        x = tp.comm.out(m, h)
+        ops.residual_norm(hh, None, None, g0, x, eps)
+        x0 = x.clone()
+        x1 = tp.layer(0, x, hh, g1, eps)
+        kept = tp.comm.rows(m, h)
+        y = None
+    else:
+        x0 = torch.empty_like(hh)
+        ops.residual_norm(hh, None, None, g0, x0, eps)
+        w = stack.layers[0]
+        y = torch.empty_like(hh)
+        ops.w4a16_ffn(y, x0, w.gate_up, w.down, w.hidden, w.channels(), w.stored_channels(), int(w.layout))
+        x1 = torch.empty_like(hh)
+        ops.residual_norm(hh, y, None, g1, x1 if g1 is not None else None, eps)
+        if g1 is None:
+            x1 = hh
+        kept = (0, m)
+    torch.cuda.synchronize(dev)
+    if rank != 0:
+        return None
+    blocks = (m + 255) // 256
+    step = max(1, blocks // n_rows)
+    rows = sorted({min(m - 1, 256 * b + (128 if (b // step) % 2 else 0) + (37 * b) % 128) for b in range(0, blocks, step)}
+                  | {0, m - 1})
+    rows = torch.tensor(rows, device=dev)
+    prev_tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        def deq(p, k, n):
+            out = torch.empty(k, n, dtype=torch.float32, device=dev)
+            ops.w4a16_dequant(out, p, k, n, k, n)
+            return out
+
+        gate_w, up_w, down_w = raw0
+        xr = x0[rows].float()
+        gate = (xr @ deq(gate_w, h, inter)).to(torch.bfloat16).float()
+        up = (xr @ deq(up_w, h, inter)).to(torch.bfloat16).float()
+        act = (gate / (1.0 + torch.exp(-gate)) * up).to(torch.bfloat16).float()
+        y_ref = act @ deq(down_w, inter, h)
+        h1_ref = (h0[rows].float() + y_ref.to(torch.bfloat16).float()).to(torch.bfloat16).float()
+        if g1 is not None:
+            x1_ref = (h1_ref * torch.rsqrt((h1_ref * h1_ref).mean(-1, keepdim=True) + eps) * g1.float()).to(torch.bfloat16)
+        else:
+            x1_ref = h1_ref.to(torch.bfloat16)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev_tf32
+
+    def metrics(got, ref):
+        got, ref = got.double(), ref.double()
+        d = got - ref
+        return {"max_rel": float(d.abs().max() / ref.abs().max()), "rel_l2": float(d.norm() / ref.norm()),
+                "cos": float((got * ref).sum() / (got.norm() * ref.norm()))}
+
+    out = {"what": "layer 0 + boundary at full M vs torch fp32 dequant-then-matmul on sampled rows",
+           "rows": int(rows.numel()), "tolerance": {"max_rel": 1e-2, "rel_l2": 1e-2, "cos": 0.9999}}
+    out["next_input"] = metrics(x1[rows].float(), x1_ref.float())
+    own = rows[(rows >= kept[0]) & (rows < kept[1])]
+    if own.numel():
+        sel = torch.isin(rows, own)
+        out["residual"] = metrics(hh[own].float(), h1_ref[sel])
+    if y is not None:
+        out["ffn"] = metrics(y[rows].float(), y_ref)
+    checks = [v for k, v in out.items() if k in ("next_input", "residual", "ffn")]
+    out["max_rel"] = max(c["max_rel"] for c in checks)
+    out["pass"] = all(c["max_rel"] <= 1e-2 and c["rel_l2"] <= 1e-2 and c["cos"] >= 0.9999 for c in checks)
+    return out
 
 
 def dominant_kernel(stack, w, x, flush, stream, m, reps=20):
@@ -424,70 +526,109 @@ def traffic_from_profiles(wl, kernel):
 
 # ---- CPU: the reference's own AVX kernel (oracle/_ref), or the oracle port ------------------------------
 
-def cpu_ffn_setup(wl, rows):
-    import numpy as np
+def physical_cores():
+    """Physical cores this process may run on (the reference's AVX kernel gains nothing from SMT)."""
+    avail = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    try:
+        import psutil
 
-    from oracle import oracle as O
-
-    h, n = wl["hidden"], wl["inter"]
-    rng = np.random.default_rng(1000)
-    gate_up = rng.integers(0, 256, (h // 128) * (2 * n // 64) * 4352, dtype=np.uint8)
-    down = rng.integers(0, 256, (n // 128) * (h // 64) * 4352, dtype=np.uint8)
-    for p, k, nn in ((gate_up, h, 2 * n), (down, n, h)):
-        t = p.reshape(-1, 4352)
-        t[:, 4096:4224] = O.bf16_bits(rng.uniform(0.002, 0.02, (t.shape[0], 64))).view(np.uint8).reshape(-1, 128)
-        z = rng.integers(0, 16, (t.shape[0], 8, 8), dtype=np.uint8)
-        t[:, 4224:] = np.concatenate([z, z], 2).reshape(-1, 128)
-    x = O.bf16_bits(np.random.default_rng(7).standard_normal((rows, h)))
-    return O, gate_up, down, x
+        phys = psutil.cpu_count(logical=False) or avail
+    except Exception:
+        phys = avail
+    return max(1, min(phys, avail))
 
 
-def cpu_layer_runner(wl, rows):
-    """A callable that runs the FFN of one layer for `rows` tokens on the host, and its description."""
-    O, gate_up, down, x = cpu_ffn_setup(wl, rows)
-    h, n = wl["hidden"], wl["inter"]
-    threads = os.cpu_count() or 1
-    if O.ReferenceAVX.available():
-        avx = O.ReferenceAVX()
+class CpuFfn:
+    """The reference model's FFN on the host for `rows` tokens through one layer
+    (src/unified_llm_w4a16_hetero/unified_llm_w4a16.cpp:2872-2887): the gate and up projections as two
+    packed [H, I] matrices, each through the reference's own CPU AVX GEMV
+    (w4a16_gemv_cpu_fused_packed, src/cpu_avx_kernels/w4a16_gemv_avx_packed.cpp, built unchanged into
+    oracle/_ref), then torch's CPU bf16 silu_ and mul_ as the model runs them, then down [I, H] through
+    the AVX GEMV, one token at a time (the reference has no CPU GEMM). Without oracle/_ref the C port
+    of the same GEMV (oracle/w4a16_oracle.c) stands in and `kind` says "port". Seeded synthetic weights
+    with the benchmark's distribution."""
 
-        def run():
-            for r in range(rows):
-                gu = avx.gemv(x[r], gate_up, h, 2 * n, threads)
-                act = O.silu_mul(gu[None, :], n, 1)[0]
-                avx.gemv(act, down, n, h, threads)
+    def __init__(self, wl, rows):
+        import numpy as np
 
-        kind = "reference"
-        what = ("w4a16_gemv_cpu_fused_packed (src/cpu_avx_kernels/w4a16_gemv_avx_packed.cpp, built unchanged, "
-                + ("AVX512-BF16" if avx.avx512 else "scalar branch: host lacks AVX512-BF16") + ")")
-    else:
-        def run():
-            O.ffn(gate_up, down, h, n, n, 1, x)
+        from oracle import oracle as O
 
-        kind = "port"
-        what = "C oracle (oracle/w4a16_oracle.c, OpenMP)"
-    return run, kind, what, threads
+        self.O, self.h, self.n, self.rows = O, wl["hidden"], wl["inter"], rows
+        rng = np.random.default_rng(1000)
+
+        def packed(k, n):
+            p = rng.integers(0, 256, (k // 128) * (n // 64) * 4352, dtype=np.uint8)
+            t = p.reshape(-1, 4352)
+            t[:, 4096:4224] = O.bf16_bits(rng.uniform(0.002, 0.02, (t.shape[0], 64))).view(np.uint8).reshape(-1, 128)
+            z = rng.integers(0, 16, (t.shape[0], 8, 8), dtype=np.uint8)
+            t[:, 4224:] = np.concatenate([z, z], 2).reshape(-1, 128)
+            return p
+
+        self.gate, self.up, self.down = packed(self.h, self.n), packed(self.h, self.n), packed(self.n, self.h)
+        self.x = O.bf16_bits(np.random.default_rng(7).standard_normal((rows, self.h)))
+        self.avx = O.ReferenceAVX() if O.ReferenceAVX.available() else None
+        if self.avx is not None:
+            self.kind = "reference"
+            self.what = ("w4a16_gemv_cpu_fused_packed (src/cpu_avx_kernels/w4a16_gemv_avx_packed.cpp, built unchanged, "
+                         + ("AVX512-BF16" if self.avx.avx512 else "scalar branch: host lacks AVX512-BF16")
+                         + ") for gate, up and down; torch CPU bf16 silu_/mul_")
+        else:
+            self.kind = "port"
+            self.what = "C port of the reference GEMV (oracle/w4a16_oracle.c) for gate, up and down; torch CPU bf16 silu_/mul_"
+
+    def _gemv(self, x, packed, k, n, threads):
+        if self.avx is not None:
+            return self.avx.gemv(x, packed, k, n, threads)
+        return self.O.gemv(packed, k, n, x[None, :])[1][0]
+
+    def run(self, threads, rows=None):
+        import numpy as np
+        import torch
+
+        torch.set_num_threads(threads)
+        for r in range(self.rows if rows is None else rows):
+            g = self._gemv(self.x[r], self.gate, self.h, self.n, threads)
+            u = self._gemv(self.x[r], self.up, self.h, self.n, threads)
+            gt = torch.from_numpy(g.view(np.int16)).view(torch.bfloat16)
+            torch.nn.functional.silu(gt, inplace=True)  # torch::silu_(gate_buf)
+            gt.mul_(torch.from_numpy(u.view(np.int16)).view(torch.bfloat16))  # gate_buf.mul_(up_buf)
+            self._gemv(gt.view(torch.int16).numpy().view(np.uint16), self.down, self.n, self.h, threads)
 
 
-def cpu_baseline(wl, m, budget_s):
-    """Rank-0 CPU baseline on a bounded sample: a few tokens through one layer, scaled to the
-    workload's tokens/s (per token, the stack takes `layers` times one layer)."""
-    rows = 1 if m <= 64 else 4
-    run, kind, what, threads = cpu_layer_runner(wl, rows)
-    run()  # warm-up
-    t0 = time.perf_counter()
-    run()
-    one = time.perf_counter() - t0
-    reps = max(3, min(200, int(budget_s / max(one, 1e-6))))
+def time_cpu(run, reps, warmup=1):
+    for _ in range(warmup):
+        run()
     times = []
     for _ in range(reps):
         t0 = time.perf_counter()
         run()
         times.append(time.perf_counter() - t0)
-    per_layer_token = statistics.median(times) / rows
-    tokens_per_s = 1.0 / (per_layer_token * wl["layers"])
-    return {"value": round(tokens_per_s, 3), "unit": "tokens/s", "cores": threads, "kind": kind,
-            "sample": f"{reps} x {rows} token(s) through one {wl['hidden']}x{wl['inter']} layer (median), "
-                      f"scaled to {wl['layers']} layer(s); {what}; {cpu_model()}"}
+    return statistics.median(times)
+
+
+def cpu_single_thread(ffn, wl, budget_s=3.0):
+    """One token through one layer on one core, repeated within a small budget."""
+    one = time_cpu(lambda: ffn.run(1, rows=1), reps=1, warmup=0)
+    reps = max(1, min(5, int(budget_s / max(one, 1e-6))))
+    t = time_cpu(lambda: ffn.run(1, rows=1), reps=reps, warmup=0)
+    return {"value": round(1.0 / (t * wl["layers"]), 4), "unit": "tokens/s", "cores": 1,
+            "sample": f"{reps} x 1 token through one layer (median {t * 1e3:.1f} ms), scaled to {wl['layers']} layer(s)"}
+
+
+def cpu_baseline(wl, m, budget_s):
+    """Rank-0 CPU baseline inside the product arm, on a bounded sample: up to 16 tokens through one
+    layer on all physical cores (and one token on one core), scaled to the workload's tokens/s."""
+    rows = min(m, 16)
+    ffn = CpuFfn(wl, rows)
+    threads = physical_cores()
+    one = time_cpu(lambda: ffn.run(threads), reps=1)
+    reps = max(3, min(50, int(budget_s / max(one, 1e-6))))
+    t = time_cpu(lambda: ffn.run(threads), reps=reps, warmup=0)
+    return {"value": round(rows / (t * wl["layers"]), 4), "unit": "tokens/s", "cores": threads, "kind": ffn.kind,
+            "extrapolated": True,
+            "sample": f"{reps} x {rows} token(s) through one {wl['hidden']}x{wl['inter']} layer (median {t * 1e3:.1f} ms), "
+                      f"scaled to {wl['layers']} layer(s) and M={m}; {ffn.what}; {threads} physical cores of {cpu_model()}",
+            "threads_1": cpu_single_thread(ffn, wl)}
 
 
 def cpu_model():
@@ -502,36 +643,47 @@ def cpu_model():
 
 
 def run_reference(args):
-    """The reference arm: the reference's CPU implementation of the path, timed on the host cores, on
-    this arm's config and metric. Rank 0 only; other ranks exit without work."""
+    """The reference arm: the reference's CPU implementation of the path (CpuFfn), timed on the host's
+    physical cores on this arm's workload, metric and config. Rank 0 only; other ranks exit without
+    work. Each step runs a measured sample, min(M, 128) tokens through one layer (the reference has no
+    CPU GEMM: prefill is M GEMVs per projection), and the tokens/s of the whole workload is
+    extrapolated from it (per token, a stack of L layers takes L times one layer); the line says so
+    and reports the sample's own time as ms_per_step."""
     world, rank, _ = dist_env()
     if rank != 0:
         return
     wl = workload(args)
     m = wl["m"]
-    rows = 1 if m <= 64 else 4
-    run, kind, what, threads = cpu_layer_runner(wl, rows)
-    layers_sampled = 1
+    rows = min(m, 128)
+    ffn = CpuFfn(wl, rows)
+    threads = physical_cores()
     for _ in range(args.warmup):
-        run()
+        ffn.run(threads)
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        run()
+        ffn.run(threads)
         times.append(time.perf_counter() - t0)
-    per_token_stack = statistics.median(times) / rows * wl["layers"] / layers_sampled
-    value = 1.0 / per_token_stack
+    sample_s = statistics.median(times)
+    value = rows / (sample_s * wl["layers"])
+    single = cpu_single_thread(ffn, wl)
     line = {
-        "metric": "ffn_tokens_per_s", "value": round(value, 3), "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_token_stack * m * 1e3, 3),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded W4A16 group-128, N(0,1) bf16)", "impl": "reference",
-        "config": {"workload": f"{wl['name']}: {wl['model']} x{wl['layers']} layers, M={m}", "hidden": wl["hidden"],
-                   "intermediate": wl["inter"], "layers": wl["layers"], "m": m, "parallelism": "host cores"},
-        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads, "kind": kind,
+        "metric": "ffn_tokens_per_s", "value": round(value, 4), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sample_s * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded W4A16 group-128 weights, N(0,1) bf16 input)", "impl": "reference",
+        "config": config_of(wl, world, not args.no_graph),
+        "extrapolated": True,
+        "sample": {"tokens": rows, "layers": 1, "ms_per_step_measured": round(sample_s * 1e3, 3),
+                   "ms_per_full_step_extrapolated": round(m / value * 1e3, 1),
+                   "note": f"each step times {rows} token(s) through one layer; value scales that to M={m} x "
+                           f"{wl['layers']} layer(s) per step"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "tokens/s", "cores": threads, "kind": ffn.kind,
+                         "extrapolated": True,
                          "sample": f"each step: {rows} token(s) through one layer, scaled to M={m} x {wl['layers']} "
-                                   f"layer(s); {what}; {cpu_model()}"},
-        "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                                   f"layer(s); {ffn.what}; {threads} physical cores of {cpu_model()}",
+                         "threads_1": single},
+        "e2e": {"value": round(value, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 

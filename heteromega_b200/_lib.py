@@ -42,6 +42,7 @@ SIGNATURES = {
                                       _int, _vp]),
     "hmb_w4a16_gemm": (_int, [_vp, _i64, _i64, _vp, _i64, _int, _vp, _i64, _int, _i64, _i64, _i64, _i64, _int, _int, _vp]),
     "hmb_w4a16_gemm_supports": (_int, [_i64, _i64, _i64, _int]),
+    "hmb_w4a16_gemm_plan": (_int, [_i64, _i64, _i64, _int, _int, _vp]),
     "hmb_w4a16_ffn": (_int, [_vp, _vp, _i64, _i64, _i64, _int, _vp, _i64, _int, _vp, _i64, _int, _i64, _vp, _sz, _vp]),
     "hmb_w4a16_ffn_workspace": (_sz, [_i64, _i64, _i64]),
     "hmb_selftest_bounded_wait": (_int, [_i64, _vp]),

@@ -32,8 +32,13 @@ inline bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintp
 // Streaming multiprocessors of the current device (cached per device).
 int sm_count();
 
-// Device address of the status word on the current device (cached per device; nullptr on error). A
-// kernel that gives up a bounded wait ORs 1 into it; hmb_device_status() reads and clears it.
+// Unique id of the current CUDA context (cuCtxGetId; 0 if it cannot be read). Device addresses that the
+// library caches per device are cached together with it and looked up again when it changes, since a
+// device's primary context (and every module address in it) is replaced after cudaDeviceReset.
+unsigned long long current_context_id();
+
+// Device address of the status word on the current device (cached per device and context; nullptr on
+// error). A kernel that gives up a bounded wait ORs 1 into it; hmb_device_status() reads and clears it.
 int *device_status_word();
 
 // Programmatic dependent launch. A kernel launched with launch_pdl() may start while the previous

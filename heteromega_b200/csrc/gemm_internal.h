@@ -45,6 +45,15 @@ int pair_clusters();
 int pair_k_splits(int64_t m, int64_t k, int64_t n);
 size_t pair_split_bytes(int64_t m, int64_t k, int64_t n);
 
+// How gemm_run schedules an m x k x n problem: the CTA-pair kernel (pair) or the one-CTA kernel, the
+// pair kernel's band order, and its K splits (split_ws: the caller gives a large enough workspace).
+struct GemmPlan {
+    bool pair;
+    int band_rows, band;
+    int k_splits, k_per_split;
+};
+GemmPlan gemm_plan(int64_t m, int64_t k, int64_t n, bool split_ws, bool scatter);
+
 // hmb_w4a16_gemm with an optional split-K workspace: split_ws (pair_split_bytes(m, k, n) bytes of
 // fp32 sums) and split_cnt (4 KB of counters, zero before the first call; the kernel leaves them
 // zero). Without them (nullptr) no K splits are used. With a scatter target (HMB_EPI_STORE, 16-bit

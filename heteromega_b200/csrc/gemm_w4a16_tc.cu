@@ -335,18 +335,62 @@ int launch(const CUtensorMap &map, const GemmArgs &a, cudaStream_t stream) {
 
 }  // namespace
 
+unsigned long long current_context_id() {
+    using GetCurrent = CUresult (*)(CUcontext *);
+    using GetId = CUresult (*)(CUcontext, unsigned long long *);
+    static GetCurrent get_current = nullptr;
+    static GetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrent>(p);
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetId>(p);
+    });
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
+
 int *device_status_word() {
     static std::mutex mu;
     static int *addr[64] = {};
+    static unsigned long long ctx[64] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return nullptr;
+    const unsigned long long id = current_context_id();
     std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
+    if (!addr[dev] || ctx[dev] != id || id == 0) {  // id 0: no context id to key on, look it up again
         void *p = nullptr;
         if (cudaGetSymbolAddress(&p, g_gemm_status) != cudaSuccess) return nullptr;
         addr[dev] = static_cast<int *>(p);
+        ctx[dev] = id;
     }
     return addr[dev];
+}
+
+GemmPlan gemm_plan(int64_t m, int64_t k, int64_t n, bool split_ws, bool scatter) {
+    GemmPlan p{};
+    // CTA pairs for m > 128, and for smaller m when K splits (which need the caller's workspace) can
+    // fill a GPU that one-CTA tiles would leave mostly idle.
+    const int splits = split_ws ? pair_k_splits(m, k, n) : 1;
+    const bool split_ok = splits > 1;
+    const bool small_grid = (m + BM - 1) / BM * (n / BN) * 2 < sm_count();
+    // or when the pair tiles fit in one round: two SMs per tile, each dequantizing half of it
+    const bool one_round = (m + 255) / 256 * (n / 256) <= pair_clusters();
+    p.pair = m > BM || (split_ok && small_grid) || (small_grid && one_round) || scatter;
+    p.k_splits = 1;
+    p.k_per_split = static_cast<int>(k / BK);
+    if (!p.pair) return p;
+    pair_band_order(m, k, n, &p.band_rows, &p.band);
+    p.k_splits = split_ok ? splits : 1;
+    const int steps = static_cast<int>(k / BK);
+    p.k_per_split = ((steps + p.k_splits - 1) / p.k_splits + 1) / 2 * 2;
+    p.k_splits = (steps + p.k_per_split - 1) / p.k_per_split;  // no empty split
+    return p;
 }
 
 int gemm_run(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const void *x, int64_t ldx, int x_dtype, void *y, int64_t ldy,
@@ -389,14 +433,8 @@ int gemm_run(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const vo
 
     const int col_stride = (epilogue == HMB_EPI_SWIGLU && layout == HMB_GATE_UP_BLOCKED) ? static_cast<int>(n / kTileN / 2) : 1;
     const bool f16 = x_dtype == HMB_FP16, swiglu = epilogue == HMB_EPI_SWIGLU;
-    // CTA pairs for m > 128, and for smaller m when K splits (which need the caller's workspace) can
-    // fill a GPU that one-CTA tiles would leave mostly idle.
-    const int splits = split_ws && split_cnt ? pair_k_splits(m, k, n) : 1;
-    const bool split_ok = splits > 1 && split_ws_bytes >= pair_split_bytes(m, k, n);
-    const bool small_grid = (m + BM - 1) / BM * (n / BN) * 2 < sm_count();
-    // or when the pair tiles fit in one round: two SMs per tile, each dequantizing half of it
-    const bool one_round = (m + 255) / 256 * (n / 256) <= pair_clusters();
-    if (m > BM || (split_ok && small_grid) || (small_grid && one_round) || sc) {
+    const GemmPlan plan = gemm_plan(m, k, n, split_ws && split_cnt && split_ws_bytes >= pair_split_bytes(m, k, n), sc != nullptr);
+    if (plan.pair) {
         PairArgs p{};
         p.packed = packed;
         p.y = y;
@@ -409,14 +447,13 @@ int gemm_run(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const vo
         p.m_blocks = static_cast<int>((m + 255) / 256);
         p.n_blocks = static_cast<int>(n / 256);
         p.num_tiles = p.m_blocks * p.n_blocks;
-        pair_band_order(m, k, n, &p.band_rows, &p.band);
+        p.band_rows = plan.band_rows;
+        p.band = plan.band;
         p.col_stride = col_stride;
         p.y_f32 = y_dtype == HMB_FP32;
         p.status = status;
-        p.k_splits = split_ok ? splits : 1;
-        const int steps = static_cast<int>(k / BK);
-        p.k_per_split = ((steps + p.k_splits - 1) / p.k_splits + 1) / 2 * 2;
-        p.k_splits = (steps + p.k_per_split - 1) / p.k_per_split;  // no empty split
+        p.k_splits = plan.k_splits;
+        p.k_per_split = plan.k_per_split;
         p.split_ws = static_cast<float *>(split_ws);
         p.split_cnt = split_cnt;
         if (sc) {
@@ -450,6 +487,18 @@ extern "C" {
 int hmb_w4a16_gemm_supports(int64_t m, int64_t k, int64_t n, int epilogue) {
     if (m <= 0 || k <= 0 || n <= 0 || k % kTileK) return 0;
     return n % BN == 0 && (epilogue == HMB_EPI_STORE || epilogue == HMB_EPI_SWIGLU) && m < (int64_t(1) << 30);
+}
+
+int hmb_w4a16_gemm_plan(int64_t m, int64_t k, int64_t n, int epilogue, int with_workspace, int *plan) {
+    if (!plan || !hmb_w4a16_gemm_supports(m, k, n, epilogue)) return HMB_ERR_ARG;
+    if (pair_clusters() <= 0) return HMB_ERR_CUDA;
+    const GemmPlan p = gemm_plan(m, k, n, with_workspace != 0, false);
+    plan[0] = p.pair ? 2 : 1;
+    plan[1] = p.pair ? p.band_rows : 0;
+    plan[2] = p.pair ? p.band : 0;
+    plan[3] = p.k_splits;
+    plan[4] = p.pair ? pair_clusters() : static_cast<int>((m + BM - 1) / BM * (n / BN));
+    return HMB_OK;
 }
 
 int hmb_w4a16_gemm(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const void *x, int64_t ldx, int x_dtype, void *y,

@@ -836,10 +836,13 @@ constexpr size_t kStaticScratchBytes = kCounterBytes + kStaticPartialBytes;
 // stand-in, not a device address: only the pointer from cudaGetSymbolAddress may reach a kernel.
 static __device__ __align__(256) uint8_t g_gemv_scratch[kStaticScratchBytes];
 
-// Device address of g_gemv_scratch for the current device, looked up once per device.
+// Device address of g_gemv_scratch for the current device, looked up once per device and context:
+// after cudaDeviceReset the device gets a new primary context, the module is loaded again and the
+// array has a new address, so a change of context id triggers a new lookup.
 int static_scratch(uint8_t **out) {
     static std::mutex mu;
     static uint8_t *addr[64] = {};
+    static unsigned long long ctx[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) {
@@ -847,8 +850,9 @@ int static_scratch(uint8_t **out) {
         return HMB_ERR_CUDA;
     }
     if (dev >= 64) return HMB_ERR_UNSUPPORTED;
+    const unsigned long long id = current_context_id();
     std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
+    if (!addr[dev] || ctx[dev] != id || id == 0) {  // id 0: no context id to key on, look it up again
         void *p = nullptr;
         e = cudaGetSymbolAddress(&p, g_gemv_scratch);
         if (e != cudaSuccess) {
@@ -856,6 +860,7 @@ int static_scratch(uint8_t **out) {
             return HMB_ERR_CUDA;
         }
         addr[dev] = static_cast<uint8_t *>(p);
+        ctx[dev] = id;
     }
     *out = addr[dev];
     return HMB_OK;

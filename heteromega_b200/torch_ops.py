@@ -141,6 +141,16 @@ def gemm_supported(m, k, n, epilogue):
     return bool(lib().hmb_w4a16_gemm_supports(m, k, n, epilogue))
 
 
+def gemm_plan(m, k, n, epilogue=0, with_workspace=False):
+    """How the GEMM schedules an m x k x n problem on the current device (hmb_w4a16_gemm_plan):
+    {"kernel": "cta" | "pair", "band_rows": bool, "band": width in blocks, "k_splits", "grid"}."""
+    import ctypes
+    plan = (ctypes.c_int * 5)()
+    check(lib().hmb_w4a16_gemm_plan(m, k, n, epilogue, int(bool(with_workspace)), plan), "w4a16_gemm_plan")
+    return {"kernel": "pair" if plan[0] == 2 else "cta", "band_rows": bool(plan[1]), "band": plan[2],
+            "k_splits": plan[3], "grid": plan[4]}
+
+
 # Rows above which the tensor-core GEMM takes over from the decode GEMV.
 GEMV_MAX_ROWS = 16
 
@@ -156,10 +166,20 @@ def w4a16_linear(out, x, packed, k, n, packed_k, packed_n, start_col=0, epilogue
 
 
 def device_status(device=None):
-    """HMB_OK, or HMB_ERR_TIMEOUT if a kernel gave up a bounded wait since the last call (clears it)."""
+    """HMB_OK, or HMB_ERR_TIMEOUT if a kernel gave up a bounded wait since the last call (clears it).
+    A kernel that gave up may have left split-K counters raised in its workspace, so on a timeout the
+    workspaces cached for this device are zero-filled again before any later call uses them."""
     import ctypes
     v = ctypes.c_int(0)
-    check(lib().hmb_device_status(ctypes.addressof(v), torch.cuda.current_stream(device).cuda_stream), "device_status")
+    stream = torch.cuda.current_stream(device)
+    check(lib().hmb_device_status(ctypes.addressof(v), stream.cuda_stream), "device_status")
+    if v.value == _lib.HMB_ERR_TIMEOUT:
+        index = stream.device.index
+        with _ws_lock:
+            for (dev_index, _, _), buf in _workspaces.items():
+                if dev_index == index:
+                    buf.zero_()
+        torch.cuda.synchronize(stream.device)
     return v.value
 
 

@@ -133,7 +133,8 @@ size_t hmb_w4a16_gemv_workspace(int64_t m, int64_t k, int64_t n, int epilogue, i
  * memory that every GPU loading libhmb.so keeps until the process exits; a call that would need more
  * (see hmb_w4a16_gemv_workspace) returns HMB_ERR_WORKSPACE before touching the device. The call
  * itself allocates nothing. The first call on a device looks up the array's device address
- * (cudaGetSymbolAddress), so make that first call before any stream capture. All calls share the one
+ * (cudaGetSymbolAddress), and so does the first call after the device's context was replaced
+ * (cudaDeviceReset), so make that first call before any stream capture. All calls share the one
  * array: each clears its counters first, and calls whose kernels overlap on the GPU (different
  * streams, or different host threads) race on it and give wrong results. */
 int hmb_w4a16_gemv_noalloc(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const void *x, int64_t ldx, int x_dtype,
@@ -150,6 +151,14 @@ int hmb_w4a16_gemm(const uint8_t *packed, int64_t packed_k, int64_t packed_n, co
                    int64_t ldy, int y_dtype, int64_t m, int64_t k, int64_t n, int64_t start_col, int epilogue, int layout,
                    hmb_stream_t stream);
 int hmb_w4a16_gemm_supports(int64_t m, int64_t k, int64_t n, int epilogue);
+/* How hmb_w4a16_gemm (with_workspace 0) or the GEMMs of hmb_w4a16_ffn (with_workspace 1) schedule an
+ * m x k x n problem on the current device, for diagnostics and tests. plan[5] receives:
+ *   [0] kernel: 1 = one CTA per 128 x 256 tile, 2 = CTA pairs (tcgen05 cta_group::2) on 256 x 256 tiles;
+ *   [1] the pair kernel's tile order: 1 = bands of [2] row blocks (x kept in L2 while the weight column
+ *       blocks stream past), 0 = bands of [2] weight column blocks; [2] = that band width in blocks;
+ *   [3] K splits per tile (1 = none); [4] CTAs (kernel 1) or CTA pairs (kernel 2) the launch keeps busy.
+ * No counterpart in the reference (its GEMMs have a fixed grid). */
+int hmb_w4a16_gemm_plan(int64_t m, int64_t k, int64_t n, int epilogue, int with_workspace, int *plan);
 
 /* One SwiGLU FFN (or the FFN slice of one rank) end to end: y[m, h] = (SiLU(x Wg) * (x Wu)) Wd over
  * channels [0, n). gate_up is the packed [h x 2 stored] matrix in `layout` order (HMB_GATE_UP_BLOCKED
@@ -235,7 +244,10 @@ int hmb_comm_out(hmb_comm *comm, void **ptr, size_t *bytes);
 int hmb_comm_rows(const hmb_comm *comm, int64_t m, int64_t h, int64_t *begin, int64_t *end);
 
 /* Reads and clears the device status word of the current device: *status = HMB_ERR_TIMEOUT if a kernel
- * gave up a bounded wait since the last call, else HMB_OK. Synchronizes `stream`. */
+ * gave up a bounded wait since the last call, else HMB_OK. Synchronizes `stream`. A kernel that gave up
+ * can leave split-K counters raised in the workspace it was given: after HMB_ERR_TIMEOUT, zero-fill
+ * every workspace (hmb_w4a16_gemv, hmb_w4a16_ffn, hmb_tp_ffn_layer) again before its next use, or its
+ * next call may pick the wrong last contributor and write wrong sums without an error. */
 int hmb_device_status(int *status, hmb_stream_t stream);
 
 /* act[m, n] = bf16(SiLU(g) * u), fp32 math, one rounding; gate_up [m, 2n] in `layout` order.

@@ -1,9 +1,9 @@
 """Generate the golden fixtures in this folder from the reference's own code.
 
-Run where the reference tree is available (its location in $HETEROMEGA_REF, else the default
-below) after ``make -C oracle ref``:
+Run where the reference tree is available, with its location in $HETEROMEGA_REF, after
+``make -C oracle ref REF=$HETEROMEGA_REF``:
 
-    python tests/golden/make_golden.py
+    HETEROMEGA_REF=<reference checkout> python tests/golden/make_golden.py
 
 It imports the reference's Python packers and oracles and runs its CPU AVX GEMV
 (compiled unchanged into oracle/_ref/), and writes small .npz fixtures that the
@@ -31,7 +31,9 @@ import sys
 
 import numpy as np
 
-REF = os.environ.get("HETEROMEGA_REF", "/root/reference")
+REF = os.environ.get("HETEROMEGA_REF")
+if not REF or not os.path.isdir(REF):
+    raise SystemExit("make_golden.py: set HETEROMEGA_REF to the reference checkout")
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
 for sub in ("kernels/gpu/tools", "experiments/ffn_partition", "npu/ffn", "py/unified_llm_w4a16"):
