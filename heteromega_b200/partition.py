@@ -5,9 +5,12 @@ HeteroMega splits the intermediate channels of each FFN layer between an NPU and
 up are cut by output columns, down by input rows, and the per-device partial outputs are summed
 once at the layer boundary. Here the same algebra runs over P B200 ranks.
 
-* FFNPartition restates the reference's two-device split and its ``from_ratio`` rounding
-  (nearest multiple of the alignment, ties upward; reference.py:139-147).
-* plan_shards generalises it to P ranks: the cumulative share of rank r is rounded the same
+* ChannelSplit holds the ranges of any number of devices as one list of boundaries. Its
+  two-device form, ChannelSplit.two_way, puts the cut where the reference's from_ratio puts it:
+  the first device's share rounded to the nearest multiple of the alignment, ties upward
+  (reference.py:139-147); that rounding rule is the one thing kept alike, so that both place the
+  same partition points.
+* plan_shards generalises the cut to P ranks: the cumulative share of rank r is rounded the same
   way, so equal shares come out when I/P is aligned and 128-aligned unequal shares otherwise
   (Qwen2.5-14B, I = 13824 over 8 ranks: 4 x 1792 + 4 x 1664).
 * predict_layer_time is the per-layer cost form of tools/split_model/split_cost_model.py:8,
@@ -16,15 +19,16 @@ once at the layer boundary. Here the same algebra runs over P B200 ranks.
 """
 import dataclasses
 import math
-from numbers import Integral
 
 ALIGNMENT = 128
 BYTES_PER_WEIGHT = 4352 / (128 * 64)  # packed tile bytes per weight: 0.53125
 
 
-def _positive_int(value, name):
-    if isinstance(value, bool) or not isinstance(value, Integral) or value <= 0:
-        raise ValueError(f"{name} must be a positive integer")
+def _count(value, what, minimum=1):
+    """value as an int >= minimum; bools and non-integral numbers are refused."""
+    if isinstance(value, bool) or int(value) != value or value < minimum:
+        raise ValueError(f"{what}: expected an integer >= {minimum}, got {value!r}")
+    return int(value)
 
 
 def round_aligned(value, alignment=ALIGNMENT):
@@ -33,41 +37,57 @@ def round_aligned(value, alignment=ALIGNMENT):
 
 
 @dataclasses.dataclass(frozen=True)
-class FFNPartition:
-    """The reference's two-way split: device "npu" owns [0, npu_channels), "gpu" the rest."""
-    intermediate_channels: int
-    npu_channels: int
+class ChannelSplit:
+    """Contiguous channel ranges of one FFN layer, one per device in device order, given by their
+    boundaries (0, b_1, ..., inter); every boundary is a multiple of `alignment`. A device may own
+    no channels (two equal neighbouring boundaries)."""
+    inter: int
+    bounds: tuple
     alignment: int = ALIGNMENT
 
     def __post_init__(self):
-        _positive_int(self.intermediate_channels, "intermediate_channels")
-        _positive_int(self.alignment, "alignment")
-        if isinstance(self.npu_channels, bool) or not isinstance(self.npu_channels, Integral):
-            raise ValueError("npu_channels must be an integer")
-        if not 0 <= self.npu_channels <= self.intermediate_channels:
-            raise ValueError("npu_channels must lie within the FFN width")
-        if self.intermediate_channels % self.alignment or self.npu_channels % self.alignment:
-            raise ValueError("FFN width and NPU channel count must satisfy alignment")
+        inter, align = _count(self.inter, "ChannelSplit.inter"), _count(self.alignment, "ChannelSplit.alignment")
+        b = tuple(_count(v, "ChannelSplit boundary", 0) for v in self.bounds)
+        if len(b) < 2 or b[0] != 0 or b[-1] != inter:
+            raise ValueError(f"ChannelSplit: boundaries must run from 0 to {inter}, got {b}")
+        if any(hi < lo for lo, hi in zip(b, b[1:])):
+            raise ValueError(f"ChannelSplit: boundaries must not decrease, got {b}")
+        if any(v % align for v in b):
+            raise ValueError(f"ChannelSplit: boundaries must be multiples of {align}, got {b}")
+        object.__setattr__(self, "bounds", b)
 
     @classmethod
-    def from_ratio(cls, intermediate_channels, npu_ratio, alignment=ALIGNMENT):
-        _positive_int(intermediate_channels, "intermediate_channels")
-        _positive_int(alignment, "alignment")
-        if not math.isfinite(npu_ratio) or not 0 <= npu_ratio <= 1:
-            raise ValueError("npu_ratio must be finite and in [0, 1]")
-        return cls(intermediate_channels, round_aligned(intermediate_channels * npu_ratio, alignment), alignment)
+    def two_way(cls, inter, first_ratio, alignment=ALIGNMENT):
+        """Two devices, the first taking `first_ratio` of the channels (the reference's NPU share),
+        its width rounded to the nearest aligned count, ties upward."""
+        r = float(first_ratio)
+        if not (0.0 <= r <= 1.0):
+            raise ValueError(f"ChannelSplit.two_way: the ratio must lie in [0, 1], got {first_ratio!r}")
+        return cls(inter, (0, round_aligned(inter * r, alignment), inter), alignment)
+
+    @classmethod
+    def balanced(cls, inter, world, ratios=None, alignment=ALIGNMENT):
+        """`world` devices with shares proportional to `ratios` (default equal), see plan_shards."""
+        shares = plan_shards(inter, world, ratios, alignment)
+        return cls(inter, tuple(b for b, _ in shares) + (inter,), alignment)
 
     @property
-    def slices(self):
-        return {"npu": (0, self.npu_channels), "gpu": (self.npu_channels, self.intermediate_channels)}
+    def devices(self):
+        return len(self.bounds) - 1
+
+    def ranges(self):
+        """[(begin, end)] per device."""
+        return list(zip(self.bounds, self.bounds[1:]))
+
+    def __getitem__(self, device):
+        return self.bounds[device], self.bounds[device + 1]
 
 
 def plan_shards(inter, world, ratios=None, alignment=ALIGNMENT):
     """[(begin, end)] channel range of each of `world` ranks. `ratios` (default: equal) are
     relative speeds; boundaries are cumulative shares rounded to the alignment, ties upward.
     Every rank gets at least one aligned block."""
-    _positive_int(inter, "inter")
-    _positive_int(world, "world")
+    inter, world = _count(inter, "plan_shards inter"), _count(world, "plan_shards world")
     if inter % alignment:
         raise ValueError(f"inter must be a multiple of {alignment}")
     if inter // alignment < world:

@@ -17,7 +17,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import heteromega_b200 as H
-from heteromega_b200.partition import DeviceModel, FFNPartition, best_ratios, plan_shards, predict_layer_time
+from heteromega_b200.partition import ChannelSplit, DeviceModel, best_ratios, plan_shards, predict_layer_time
 from heteromega_b200.tensor_parallel import TensorParallelFfn
 from heteromega_b200.weights import synthetic_layer
 
@@ -31,12 +31,22 @@ def free_port():
 
 
 def test_from_ratio_matches_reference(golden):
+    """The two-device cut lands where the reference's FFNPartition.from_ratio puts the NPU share."""
     for inter, ratio, npu in golden("contract")["from_ratio"]:
-        assert FFNPartition.from_ratio(int(inter), float(ratio)).npu_channels == int(npu)
+        split = ChannelSplit.two_way(int(inter), float(ratio))
+        assert split[0] == (0, int(npu)) and split[1] == (int(npu), int(inter))
     with pytest.raises(ValueError):
-        FFNPartition.from_ratio(14336, 1.5)
+        ChannelSplit.two_way(14336, 1.5)
     with pytest.raises(ValueError):
-        FFNPartition(14336, 100)
+        ChannelSplit(14336, (0, 100, 14336))
+    with pytest.raises(ValueError):
+        ChannelSplit(14336, (0, 8192, 4096, 14336))
+
+
+@pytest.mark.parametrize("inter,world", [(14336, 8), (13824, 8), (13824, 3)])
+def test_channel_split_balanced_matches_plan(inter, world):
+    split = ChannelSplit.balanced(inter, world)
+    assert split.devices == world and split.ranges() == plan_shards(inter, world)
 
 
 @pytest.mark.parametrize("inter,world", [(8192, 2), (14336, 8), (13824, 8), (28672, 8), (13824, 3), (1024, 8)])
