@@ -1,9 +1,12 @@
 """Builds libhmb.so in-tree with nvcc for sm_100a (B200). No GPU needed: nvcc cross-compiles.
 
-    python -m heteromega_b200.build [--verbose] [--ptxas-info]
+    python -m heteromega_b200.build [--verbose] [--ptxas-info] [--reference DIR]
 
 Objects go to heteromega_b200/_build/, the library to heteromega_b200/libhmb.so. Sources
-are compiled in parallel and only when they (or the headers) changed.
+are compiled in parallel and only when they (or the headers) changed. With the reference
+checkout given (--reference, or $HETEROMEGA_REF), the C++ drop-in of its FFN interface
+(cpp/gpu_ffn_dropin.cpp -> libhmb_dropin.so) and its C++ self-test are built against the
+reference's own headers as well.
 """
 import argparse
 import concurrent.futures as cf
@@ -71,11 +74,21 @@ def build(verbose=False, ptxas_info=False, force=False):
     return LIB
 
 
+def build_dropin(reference):
+    """libhmb_dropin.so and tests/cpp/_build/dropin_selftest, compiled against the reference's headers."""
+    for folder in (os.path.join(PKG, "cpp"), os.path.join(REPO, "tests", "cpp")):
+        subprocess.run(["make", "-s", "-C", folder, f"REF={reference}", f"PY={sys.executable}"], check=True)
+    return os.path.join(PKG, "libhmb_dropin.so")
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--ptxas-info", action="store_true")
     ap.add_argument("--force", action="store_true")
+    ap.add_argument("--reference", default=os.environ.get("HETEROMEGA_REF", ""))
     args = ap.parse_args()
     print(build(args.verbose, args.ptxas_info, args.force))
+    if args.reference:
+        print(build_dropin(args.reference))
     sys.exit(0)
