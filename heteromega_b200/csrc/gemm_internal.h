@@ -45,13 +45,43 @@ int pair_clusters();
 int pair_k_splits(int64_t m, int64_t k, int64_t n);
 size_t pair_split_bytes(int64_t m, int64_t k, int64_t n);
 
-// How gemm_run schedules an m x k x n problem: the CTA-pair kernel (pair) or the one-CTA kernel, the
-// pair kernel's band order, and its K splits (split_ws: the caller gives a large enough workspace).
+// Arguments of the swap-AB kernel for 17 to 128 rows (gemm_w4a16_skinny.cu).
+struct SkinnyArgs {
+    const uint8_t *packed;
+    void *y;
+    int64_t ldy;
+    int tiles_k_total, tiles_n_total;
+    int col_tile0;
+    int col_stride;      // SwiGLU blocked layout: tile columns from gate to up; 1 = interleaved
+    int tiles;           // K / 128 (packed tile rows; two steps of 64 each)
+    int blocks;          // column blocks of 128 weight columns (SwiGLU: 64 channels)
+    int m, nt;           // rows of x; the MMA's N (a multiple of 16, >= m, <= 128)
+    int y_f32;           // HMB_EPI_STORE: write the fp32 sums instead of rounding them
+    int streamk;         // 1: equal shares of the (block, step) units, split blocks summed in `partial`
+    float *partial;      // streamk: 2 slots per CTA of 128 x 128 fp32
+    unsigned *counters;  // streamk: one per block, zero before the call, left zero
+    int *status;         // device status word (1 after a wait gave up)
+};
+
+// Whether the swap-AB kernel takes an m x k x n problem, its grid, and the workspace bytes of its
+// stream-K partial sums.
+bool skinny_supported(int64_t m, int64_t k, int64_t n);
+int skinny_ctas(int64_t m, int64_t k, int64_t n, bool streamk);
+size_t skinny_split_bytes(int64_t m, int64_t k, int64_t n);
+// Launches it; `map` is x as a 2D tensor map with 64 x nt boxes (SWIZZLE_128B).
+int launch_gemm_skinny(const CUtensorMap &map, const SkinnyArgs &a, bool f16, int epilogue, cudaStream_t stream);
+
+// How gemm_run schedules an m x k x n problem: the swap-AB kernel (skinny, 17 to 128 rows), the
+// CTA-pair kernel (pair) or the one-CTA kernel; the pair kernel's band order and its K splits
+// (split_ws: the caller gives a large enough workspace); the skinny kernel's stream-K mode.
 struct GemmPlan {
+    bool skinny, streamk;
     bool pair;
     int band_rows, band;
     int k_splits, k_per_split;
 };
+// Workspace bytes that gemm_run's split-K and stream-K modes use for an m x k x n problem.
+size_t gemm_split_bytes(int64_t m, int64_t k, int64_t n);
 GemmPlan gemm_plan(int64_t m, int64_t k, int64_t n, bool split_ws, bool scatter);
 
 // hmb_w4a16_gemm with an optional split-K workspace: split_ws (pair_split_bytes(m, k, n) bytes of

@@ -372,8 +372,19 @@ int *device_status_word() {
     return addr[dev];
 }
 
+size_t gemm_split_bytes(int64_t m, int64_t k, int64_t n) { return std::max(pair_split_bytes(m, k, n), skinny_split_bytes(m, k, n)); }
+
 GemmPlan gemm_plan(int64_t m, int64_t k, int64_t n, bool split_ws, bool scatter) {
     GemmPlan p{};
+    // 17 to 128 rows: the swap-AB kernel (weights as the MMA's A operand in TMEM); stream-K shares
+    // with a workspace (and at most one counter per block in the 4 KB counter area).
+    if (skinny_supported(m, k, n) && !scatter) {
+        p.skinny = true;
+        p.streamk = split_ws && n / 128 <= static_cast<int64_t>(kSplitCounterBytes / sizeof(unsigned));
+        p.k_splits = 1;
+        p.k_per_split = static_cast<int>(k / BK);
+        return p;
+    }
     // CTA pairs for m > 128, and for smaller m when K splits (which need the caller's workspace) can
     // fill a GPU that one-CTA tiles would leave mostly idle.
     const int splits = split_ws ? pair_k_splits(m, k, n) : 1;
@@ -433,7 +444,34 @@ int gemm_run(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const vo
 
     const int col_stride = (epilogue == HMB_EPI_SWIGLU && layout == HMB_GATE_UP_BLOCKED) ? static_cast<int>(n / kTileN / 2) : 1;
     const bool f16 = x_dtype == HMB_FP16, swiglu = epilogue == HMB_EPI_SWIGLU;
-    const GemmPlan plan = gemm_plan(m, k, n, split_ws && split_cnt && split_ws_bytes >= pair_split_bytes(m, k, n), sc != nullptr);
+    const GemmPlan plan = gemm_plan(m, k, n, split_ws && split_cnt && split_ws_bytes >= gemm_split_bytes(m, k, n), sc != nullptr);
+    if (plan.skinny) {
+        SkinnyArgs sa{};
+        sa.packed = packed;
+        sa.y = y;
+        sa.ldy = ldy;
+        sa.tiles_k_total = static_cast<int>(packed_k / kTileK);
+        sa.tiles_n_total = static_cast<int>(packed_n / kTileN);
+        sa.col_tile0 = static_cast<int>(start_col / kTileN);
+        sa.col_stride = col_stride;
+        sa.tiles = static_cast<int>(k / kTileK);
+        sa.blocks = static_cast<int>(n / 128);
+        sa.m = static_cast<int>(m);
+        sa.nt = static_cast<int>((m + 15) / 16 * 16);
+        sa.y_f32 = y_dtype == HMB_FP32;
+        sa.streamk = plan.streamk ? 1 : 0;
+        sa.partial = static_cast<float *>(split_ws);
+        sa.counters = split_cnt;
+        sa.status = status;
+        // x in 64 x nt boxes: rows past m read as zeros.
+        CUtensorMap smap;
+        const cuuint32_t sbox[2] = {BK, static_cast<cuuint32_t>(sa.nt)};
+        const CUresult scr = encode(&smap, x_dtype == HMB_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                                    const_cast<void *>(x), dims, strides, sbox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (scr != CUDA_SUCCESS) return HMB_ERR_ARG;
+        return launch_gemm_skinny(smap, sa, f16, epilogue, stream);
+    }
     if (plan.pair) {
         PairArgs p{};
         p.packed = packed;
@@ -486,13 +524,22 @@ extern "C" {
 
 int hmb_w4a16_gemm_supports(int64_t m, int64_t k, int64_t n, int epilogue) {
     if (m <= 0 || k <= 0 || n <= 0 || k % kTileK) return 0;
-    return n % BN == 0 && (epilogue == HMB_EPI_STORE || epilogue == HMB_EPI_SWIGLU) && m < (int64_t(1) << 30);
+    return (n % BN == 0 || skinny_supported(m, k, n)) && (epilogue == HMB_EPI_STORE || epilogue == HMB_EPI_SWIGLU) &&
+           m < (int64_t(1) << 30);
 }
 
 int hmb_w4a16_gemm_plan(int64_t m, int64_t k, int64_t n, int epilogue, int with_workspace, int *plan) {
     if (!plan || !hmb_w4a16_gemm_supports(m, k, n, epilogue)) return HMB_ERR_ARG;
     if (pair_clusters() <= 0) return HMB_ERR_CUDA;
     const GemmPlan p = gemm_plan(m, k, n, with_workspace != 0, false);
+    if (p.skinny) {
+        plan[0] = 3;
+        plan[1] = p.streamk ? 1 : 0;
+        plan[2] = 0;
+        plan[3] = 1;
+        plan[4] = skinny_ctas(m, k, n, p.streamk);
+        return HMB_OK;
+    }
     plan[0] = p.pair ? 2 : 1;
     plan[1] = p.pair ? p.band_rows : 0;
     plan[2] = p.pair ? p.band : 0;

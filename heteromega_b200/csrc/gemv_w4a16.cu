@@ -65,6 +65,7 @@ struct GemvArgs {
     int items;  // colsets * NCOL * k_tiles
     int warps;  // warps that share the items
     int *status;  // device status word: 1 after a bounded wait gave up
+    uint32_t shr4_mul;  // 2^28: p >> 4 as the high word of p * 2^28 (see tile_mma)
 };
 
 template <bool F16>
@@ -156,9 +157,14 @@ __device__ __forceinline__ void mma16816_zc(float (&d)[4], uint32_t a0, uint32_t
 // wlane: offset of the lane's 16 bytes in each 512-byte weight chunk of the tile.
 // xrow[mt]: shared address of this lane's x row for token block mt (rows past m repeat row m-1; their
 // results are never stored).
+// The nibble unpack keeps the ALU pipe (PRMT, LOP3, shifts) busy while the FMA pipe has room: the
+// shift of the high nibbles, p >> 4, runs there as the high word of p * 2^28. The multiplier comes from
+// the kernel arguments, so the compiler cannot turn the multiplication back into a shift.
+__device__ __forceinline__ uint32_t shr4_on_fma(uint32_t p, uint32_t mul) { return __umulhi(p, mul); }
+
 template <int MT, bool F16>
 __device__ __forceinline__ void tile_mma(uint32_t st, uint32_t wlane, const uint32_t (&xrow)[MT], int g,
-                                         float (&acc)[MT][4][4]) {
+                                         float (&acc)[MT][4][4], uint32_t shr4_mul) {
     constexpr uint32_t kMagic = F16 ? 0x64006400u : 0x43004300u;
     constexpr uint32_t kOnes = F16 ? 0x3C003C00u : 0x3F803F80u;
     constexpr float kOffset = F16 ? 1024.0f : 128.0f;
@@ -191,8 +197,8 @@ __device__ __forceinline__ void tile_mma(uint32_t st, uint32_t wlane, const uint
             const uint32_t a2 = and_or(q, kMask, kMagic);  // column 2b, rows 4t+2, 4t+3
             // Column 2b+1 (high nibbles). fp16 keeps them in place: 1024 + 16 q is exact in its 10-bit
             // mantissa, and the fold divides by 16. bf16 has 7 mantissa bits, so the nibble moves down.
-            const uint32_t a1 = F16 ? and_or(p, kMaskHi, kMagic) : and_or(p >> 4, kMask, kMagic);
-            const uint32_t a3 = F16 ? and_or(q, kMaskHi, kMagic) : and_or(q >> 4, kMask, kMagic);
+            const uint32_t a1 = F16 ? and_or(p, kMaskHi, kMagic) : and_or(shr4_on_fma(p, shr4_mul), kMask, kMagic);
+            const uint32_t a3 = F16 ? and_or(q, kMaskHi, kMagic) : and_or(shr4_on_fma(q, shr4_mul), kMask, kMagic);
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) {
                 if (j == 0) {
@@ -492,7 +498,7 @@ struct GemvWarp {
                 ++in_use;
             }
             cp_async_commit();
-            tile_mma<MT, F16>(stage_addr(use), wlane, xrow, g, acc);
+            tile_mma<MT, F16>(stage_addr(use), wlane, xrow, g, acc, a.shr4_mul);
             const int j0 = cur.j, s0 = cur.s;
             cur.next(a.k_tiles, NCOL);
             const bool set_done = cur.j != j0 || it + 1 == e;
@@ -628,6 +634,7 @@ int gemv_args(GemvArgs &a, size_t &partial, const uint8_t *packed, int64_t packe
     if (!aligned(packed, 16)) return HMB_ERR_ALIGN;
     if (packed_k / kTileK > (1 << 30) || packed_n / kTileN > (1 << 30)) return HMB_ERR_UNSUPPORTED;
     a = GemvArgs{};
+    a.shr4_mul = 1u << 28;
     a.packed = packed;
     a.tiles_k_total = static_cast<int>(packed_k / kTileK);
     a.tiles_n_total = static_cast<int>(packed_n / kTileN);
@@ -708,7 +715,7 @@ size_t hmb_w4a16_ffn_workspace(int64_t m, int64_t h, int64_t n) {
     const size_t decode = round256(partial_bytes(rows, n / kTileN, 2, grid_warps(gu_items, 0, rows))) +
                           round256(partial_bytes(rows, h / kTileN, 1, grid_warps(dn_items, 0, rows)));
     size_t prefill = 0;
-    if (m > 16) prefill = std::max(pair_split_bytes(m, h, 2 * n), pair_split_bytes(m, n, h));
+    if (m > 16) prefill = std::max(gemm_split_bytes(m, h, 2 * n), gemm_split_bytes(m, n, h));
     return kFfnControlBytes + round256(static_cast<size_t>(m) * n * 2) + std::max(decode, prefill);
 }
 

@@ -143,10 +143,13 @@ def gemm_supported(m, k, n, epilogue):
 
 def gemm_plan(m, k, n, epilogue=0, with_workspace=False):
     """How the GEMM schedules an m x k x n problem on the current device (hmb_w4a16_gemm_plan):
-    {"kernel": "cta" | "pair", "band_rows": bool, "band": width in blocks, "k_splits", "grid"}."""
+    {"kernel": "cta" | "pair", "band_rows": bool, "band": width in blocks, "k_splits", "grid"}, or
+    {"kernel": "skinny", "streamk": bool, "k_splits", "grid"} for the swap-AB kernel of 17 to 128 rows."""
     import ctypes
     plan = (ctypes.c_int * 5)()
     check(lib().hmb_w4a16_gemm_plan(m, k, n, epilogue, int(bool(with_workspace)), plan), "w4a16_gemm_plan")
+    if plan[0] == 3:
+        return {"kernel": "skinny", "streamk": bool(plan[1]), "k_splits": plan[3], "grid": plan[4]}
     return {"kernel": "pair" if plan[0] == 2 else "cta", "band_rows": bool(plan[1]), "band": plan[2],
             "k_splits": plan[3], "grid": plan[4]}
 

@@ -143,7 +143,9 @@ int hmb_w4a16_gemv_noalloc(const uint8_t *packed, int64_t packed_k, int64_t pack
 
 /* Prefill GEMM on the tcgen05 tensor cores (TMA-fed, TMEM accumulator), same operands and epilogues
  * as hmb_w4a16_gemv (y_dtype: x_dtype, or HMB_FP32 for HMB_EPI_STORE): the weights are dequantized to bf16((q - z) * s) in shared memory, products
- * accumulate in fp32, the output rounds once. Needs n % 256 == 0 (HMB_ERR_UNSUPPORTED otherwise,
+ * accumulate in fp32, the output rounds once. For 17 to 128 rows and n % 128 == 0 the weights are the MMA's
+ * A operand in TMEM (the batch range where the weight stream, not the MMA, sets the pace).
+ * Needs n % 256 == 0, or n % 128 == 0 for 17 to 128 rows (HMB_ERR_UNSUPPORTED otherwise,
  * see hmb_w4a16_gemm_supports); any m. Replaces hipkernels::w4a16_gemm_fused_packed and
  * w4a16_gemm_fused_packed_tiles with fuse_activation (include/hipkernels/w4a16_gemm_packed.hpp:38-48) and
  * heteromega::gemm_w4a16 (gpu_ffn.hpp:101-107). */
@@ -153,10 +155,13 @@ int hmb_w4a16_gemm(const uint8_t *packed, int64_t packed_k, int64_t packed_n, co
 int hmb_w4a16_gemm_supports(int64_t m, int64_t k, int64_t n, int epilogue);
 /* How hmb_w4a16_gemm (with_workspace 0) or the GEMMs of hmb_w4a16_ffn (with_workspace 1) schedule an
  * m x k x n problem on the current device, for diagnostics and tests. plan[5] receives:
- *   [0] kernel: 1 = one CTA per 128 x 256 tile, 2 = CTA pairs (tcgen05 cta_group::2) on 256 x 256 tiles;
- *   [1] the pair kernel's tile order: 1 = bands of [2] row blocks (x kept in L2 while the weight column
- *       blocks stream past), 0 = bands of [2] weight column blocks; [2] = that band width in blocks;
- *   [3] K splits per tile (1 = none); [4] CTAs (kernel 1) or CTA pairs (kernel 2) the launch keeps busy.
+ *   [0] kernel: 1 = one CTA per 128 x 256 tile, 2 = CTA pairs (tcgen05 cta_group::2) on 256 x 256 tiles,
+ *       3 = the swap-AB kernel of 17 to 128 rows (dequantized weights as the MMA's A operand in TMEM);
+ *   [1] kernel 2: the tile order, 1 = bands of [2] row blocks (x kept in L2 while the weight column
+ *       blocks stream past), 0 = bands of [2] weight column blocks; kernel 3: 1 = stream-K shares of
+ *       the (column block, K step) units (needs the workspace), 0 = whole column blocks;
+ *   [2] kernel 2: that band width in blocks; [3] K splits per tile (1 = none);
+ *   [4] CTAs (kernels 1 and 3) or CTA pairs (kernel 2) the launch keeps busy.
  * No counterpart in the reference (its GEMMs have a fixed grid). */
 int hmb_w4a16_gemm_plan(int64_t m, int64_t k, int64_t n, int epilogue, int with_workspace, int *plan);
 
