@@ -65,7 +65,6 @@ struct GemvArgs {
     int items;  // colsets * NCOL * k_tiles
     int warps;  // warps that share the items
     int *status;  // device status word: 1 after a bounded wait gave up
-    uint32_t shr4_mul;  // 2^28: p >> 4 as the high word of p * 2^28 (see tile_mma)
 };
 
 template <bool F16>
@@ -157,14 +156,9 @@ __device__ __forceinline__ void mma16816_zc(float (&d)[4], uint32_t a0, uint32_t
 // wlane: offset of the lane's 16 bytes in each 512-byte weight chunk of the tile.
 // xrow[mt]: shared address of this lane's x row for token block mt (rows past m repeat row m-1; their
 // results are never stored).
-// The nibble unpack keeps the ALU pipe (PRMT, LOP3, shifts) busy while the FMA pipe has room: the
-// shift of the high nibbles, p >> 4, runs there as the high word of p * 2^28. The multiplier comes from
-// the kernel arguments, so the compiler cannot turn the multiplication back into a shift.
-__device__ __forceinline__ uint32_t shr4_on_fma(uint32_t p, uint32_t mul) { return __umulhi(p, mul); }
-
 template <int MT, bool F16>
 __device__ __forceinline__ void tile_mma(uint32_t st, uint32_t wlane, const uint32_t (&xrow)[MT], int g,
-                                         float (&acc)[MT][4][4], uint32_t shr4_mul) {
+                                         float (&acc)[MT][4][4]) {
     constexpr uint32_t kMagic = F16 ? 0x64006400u : 0x43004300u;
     constexpr uint32_t kOnes = F16 ? 0x3C003C00u : 0x3F803F80u;
     constexpr float kOffset = F16 ? 1024.0f : 128.0f;
@@ -197,8 +191,8 @@ __device__ __forceinline__ void tile_mma(uint32_t st, uint32_t wlane, const uint
             const uint32_t a2 = and_or(q, kMask, kMagic);  // column 2b, rows 4t+2, 4t+3
             // Column 2b+1 (high nibbles). fp16 keeps them in place: 1024 + 16 q is exact in its 10-bit
             // mantissa, and the fold divides by 16. bf16 has 7 mantissa bits, so the nibble moves down.
-            const uint32_t a1 = F16 ? and_or(p, kMaskHi, kMagic) : and_or(shr4_on_fma(p, shr4_mul), kMask, kMagic);
-            const uint32_t a3 = F16 ? and_or(q, kMaskHi, kMagic) : and_or(shr4_on_fma(q, shr4_mul), kMask, kMagic);
+            const uint32_t a1 = F16 ? and_or(p, kMaskHi, kMagic) : and_or(p >> 4, kMask, kMagic);
+            const uint32_t a3 = F16 ? and_or(q, kMaskHi, kMagic) : and_or(q >> 4, kMask, kMagic);
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt) {
                 if (j == 0) {
@@ -498,7 +492,7 @@ struct GemvWarp {
                 ++in_use;
             }
             cp_async_commit();
-            tile_mma<MT, F16>(stage_addr(use), wlane, xrow, g, acc, a.shr4_mul);
+            tile_mma<MT, F16>(stage_addr(use), wlane, xrow, g, acc);
             const int j0 = cur.j, s0 = cur.s;
             cur.next(a.k_tiles, NCOL);
             const bool set_done = cur.j != j0 || it + 1 == e;
@@ -634,7 +628,6 @@ int gemv_args(GemvArgs &a, size_t &partial, const uint8_t *packed, int64_t packe
     if (!aligned(packed, 16)) return HMB_ERR_ALIGN;
     if (packed_k / kTileK > (1 << 30) || packed_n / kTileN > (1 << 30)) return HMB_ERR_UNSUPPORTED;
     a = GemvArgs{};
-    a.shr4_mul = 1u << 28;
     a.packed = packed;
     a.tiles_k_total = static_cast<int>(packed_k / kTileK);
     a.tiles_n_total = static_cast<int>(packed_n / kTileN);
