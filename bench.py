@@ -315,6 +315,9 @@ def run_hmb(args):
     from heteromega_b200.torch_ops import GEMV_MAX_ROWS
 
     decode = m <= GEMV_MAX_ROWS
+    # The metric's decode term on the same stack and weights: one token per step (prefill lines only).
+    decode_rec = None if decode else decode_record(stack, wl, args, barrier, world, dev, stream, pk["hbm_gbs"], pk_kind)
+    trace("decode record done")
     if decode:
         achieved = dom["bytes"] / (dom["ms"] * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
@@ -345,6 +348,8 @@ def run_hmb(args):
         "gpu_launches": stack.kernels_per_step() * args.steps,
         "parity": parity,
     }
+    if decode_rec is not None:
+        line["decode"] = decode_rec
     if rank == 0 and world == 1:
         line["cpu_baseline"] = cpu_baseline(wl, m, args.cpu_sample_s)
     torch.cuda.synchronize()
@@ -511,6 +516,42 @@ def end_to_end(stack, h0, m, args, flush, barrier, world, dev):
     nbytes = x_host.numel() * x_host.element_size()
     return {"value": round(m / (ms * 1e-3), 2), "unit": "tokens/s", "h2d_bytes_per_step": nbytes,
             "d2h_bytes_per_step": nbytes, "ms_per_step": round(ms, 5), "api": "FfnStack.forward_host"}
+
+
+def decode_record(stack, wl, args, barrier, world, dev, stream, hbm_gbs, peak_kind):
+    """Decode on the benchmark's stack: M = 1 through every layer (the same weights, norms and, with
+    N > 1, the same communicator), replayed as its own CUDA graph; max(3, W) warm-up steps, then K
+    timed steps with CUDA events, max over ranks. The weights exceed L2, so no flush is needed. GB/s
+    counts each layer's packed bytes (scales and zeros included) once per step, against the measured
+    copy bandwidth."""
+    import torch
+    import torch.distributed as dist
+
+    L, h, inter = wl["layers"], wl["hidden"], wl["inter"]
+    graph, g_in, _ = stack.graph(1, slot=1)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(8)
+    g_in.copy_(torch.randn(1, h, device=dev, generator=gen).to(torch.bfloat16))
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        graph.replay()
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms = start.elapsed_time(end) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    gbs = L * layer_bytes(h, inter, 1) / world / (ms * 1e-3) / 1e9
+    return {"m": 1, "steps": args.steps, "ms_per_step": round(ms, 5), "us_per_layer": round(ms * 1e3 / L, 2),
+            "tokens_per_s": round(1.0 / (ms * 1e-3), 2), "hbm_gbs_per_gpu": round(gbs, 1),
+            "frac": round(gbs / hbm_gbs, 4), "peak": hbm_gbs, "peak_source": f"of {peak_kind}"}
 
 
 def traffic_from_profiles(wl, kernel):

@@ -61,6 +61,8 @@ struct SkinnyArgs {
     float *partial;      // streamk: 2 slots per CTA of 128 x 128 fp32
     unsigned *counters;  // streamk: one per block, zero before the call, left zero
     int *status;         // device status word (1 after a wait gave up)
+    int scatter;         // HMB_EPI_STORE only: rows go to the receive slots of `sc` instead of y
+    ScatterTarget sc;
 };
 
 // Whether the swap-AB kernel takes an m x k x n problem, its grid, and the workspace bytes of its

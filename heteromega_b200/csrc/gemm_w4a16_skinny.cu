@@ -26,8 +26,9 @@
 // step of a 70B gate/up launch at 64 rows (clock64 per role in CTA 0): the x tile arrives about 3,700
 // cycles after its TMA and the ring holds 8 steps, which sets a step to about 750 cycles; the MMA
 // thread needs about 320 cycles to issue a step's 4 MMAs and commit, and a dequant warp about 630.
-// The x tile is re-read from L2 by every SM for each of its blocks (at 64 rows that is about twice the
-// weight bytes), and that stream, not HBM, is the limit of this kernel.
+// The x tile is re-read from L2 by every SM for each of its blocks (at 64 rows about twice the weight
+// bytes). A variant that fed up to four blocks from one x tile cut that stream by four but the launch
+// only by 15%: the pace is set by the latency of the dequant warps' chains and of MMA issue, not HBM.
 //
 // Roles in a CTA of 15 warps:
 //   warp 0      TMA of the x tile [nt tokens x 64] of each step;
@@ -142,6 +143,21 @@ __host__ __device__ constexpr uint32_t idesc_swap(bool f16, int n) {
 template <bool F16>
 __device__ __forceinline__ float round_out(float v) {
     return round16<F16>(v);
+}
+
+// One output (HMB_EPI_STORE) at column col of row tok: into y (fp32 or rounded), or rounded over
+// NVLink into the receive slots of a tensor-parallel communicator (every rank's, or the row owner's).
+template <bool F16>
+__device__ __forceinline__ void store_out(const SkinnyArgs &a, int par, int tok, int col, float v) {
+    if (a.scatter) {
+        const uint16_t h = static_cast<uint16_t>(to16<F16>(v));
+        const int nd = scatter_count(a.sc);
+        for (int d = 0; d < nd; ++d) scatter_row(a.sc, par, tok, d)[col] = h;
+    } else if (a.y_f32) {
+        static_cast<float *>(a.y)[static_cast<int64_t>(tok) * a.ldy + col] = v;
+    } else {
+        static_cast<uint16_t *>(a.y)[static_cast<int64_t>(tok) * a.ldy + col] = static_cast<uint16_t>(to16<F16>(v));
+    }
 }
 
 template <bool F16, int EPI>
@@ -355,6 +371,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_skinny_kernel(const __grid_c
         const int q = warp & 3;
         const int col = lane_column(q, lane);
         pdl_wait();
+        // With a scatter target: the parity of the boundary call that will read the slots (the
+        // communicator's earlier calls have completed once pdl_wait returns).
+        const int par = a.scatter ? scatter_parity(a.sc) : 0;
         const int P = gridDim.x, c = blockIdx.x;
         const int64_t total = static_cast<int64_t>(a.blocks) * a.tiles;
         int t = 0;
@@ -410,11 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_skinny_kernel(const __grid_c
                     for (int e = 0; e < 32; ++e) {
                         const int tok = c0 + e;
                         if (tok >= a.m) break;
-                        if (a.y_f32)
-                            static_cast<float *>(a.y)[static_cast<int64_t>(tok) * a.ldy + 128 * b + col] = __uint_as_float(v[e]);
-                        else
-                            static_cast<uint16_t *>(a.y)[static_cast<int64_t>(tok) * a.ldy + 128 * b + col] =
-                                static_cast<uint16_t>(to16<F16>(__uint_as_float(v[e])));
+                        store_out<F16>(a, par, tok, 128 * b + col, __uint_as_float(v[e]));
                     }
                 }
             }
@@ -474,15 +489,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_skinny_kernel(const __grid_c
                     for (int e = 0; e < 32; ++e) {
                         const int tok = c0 + e;
                         if (tok >= a.m) break;
-                        if (a.y_f32)
-                            static_cast<float *>(a.y)[static_cast<int64_t>(tok) * a.ldy + 128 * b + col] = sum[e];
-                        else
-                            static_cast<uint16_t *>(a.y)[static_cast<int64_t>(tok) * a.ldy + 128 * b + col] = static_cast<uint16_t>(to16<F16>(sum[e]));
+                        store_out<F16>(a, par, tok, 128 * b + col, sum[e]);
                     }
                 }
             }
             if (q == 0 && lane == 0) atomicExch(a.counters + b, 0u);  // ready for the next call
         }
+        // Stores into peers' slots are visible at system scope before the boundary kernel that
+        // follows this grid raises its flags.
+        if (a.scatter) __threadfence_system();
     }
 
     fence_before_sync();

@@ -378,7 +378,7 @@ GemmPlan gemm_plan(int64_t m, int64_t k, int64_t n, bool split_ws, bool scatter)
     GemmPlan p{};
     // 17 to 128 rows: the swap-AB kernel (weights as the MMA's A operand in TMEM); stream-K shares
     // with a workspace (and at most one counter per block in the 4 KB counter area).
-    if (skinny_supported(m, k, n) && !scatter) {
+    if (skinny_supported(m, k, n)) {
         p.skinny = true;
         p.streamk = split_ws && n / 128 <= static_cast<int64_t>(kSplitCounterBytes / sizeof(unsigned));
         p.k_splits = 1;
@@ -463,6 +463,10 @@ int gemm_run(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const vo
         sa.partial = static_cast<float *>(split_ws);
         sa.counters = split_cnt;
         sa.status = status;
+        if (sc) {
+            sa.scatter = 1;
+            sa.sc = *sc;
+        }
         // x in 64 x nt boxes: rows past m read as zeros.
         CUtensorMap smap;
         const cuuint32_t sbox[2] = {BK, static_cast<cuuint32_t>(sa.nt)};

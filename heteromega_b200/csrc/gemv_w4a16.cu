@@ -300,21 +300,22 @@ struct Cursor {
 // One warp's share of a GEMV: its contiguous chunk of items, streamed through its private ring.
 // prefetch() requests the weight tiles of the first S - 1 items (they never depend on an earlier
 // kernel); start() requests their rows of x; run() consumes the chunk and finishes its column sets.
-// `use0` is the warp's ring use count so far (0 for a fresh ring): a kernel that ran another GEMV
-// through the same ring continues its barriers' phases from there.
+// Ring stages have the size of the kernel's largest m (a compile-time constant), and the ring position
+// and barrier phase are wrap-around counters, so the per-tile address arithmetic needs no division.
 template <int NCOL, int MT, int W, int S, int MAXM, bool F16, int EPI>
 struct GemvWarp {
+    static constexpr int kSb = stage_bytes(MAXM);
     const GemvArgs &a;
-    int lane, g, t, gw, b, e, per_set, sb;
+    int lane, g, t, gw, b, e, per_set;
     uint32_t smem_base, ring, wlane, bars;
     int64_t x_src[(16 * MAXM + 31) / 32];
     uint32_t x_dst[(16 * MAXM + 31) / 32];
     uint32_t xrow[MT];
     Cursor in;
     const uint8_t *in_col;
-    int use0, in_use;
+    int in_slot;  // ring stage of the next copy
 
-    __device__ __forceinline__ GemvWarp(const GemvArgs &args, int use_start) : a(args), use0(use_start), in_use(use_start) {
+    __device__ __forceinline__ GemvWarp(const GemvArgs &args) : a(args), in_slot(0) {
         const int warp = threadIdx.x >> 5;
         lane = threadIdx.x & 31;
         g = lane >> 2;
@@ -324,12 +325,11 @@ struct GemvWarp {
         b = gw < a.warps ? static_cast<int>(static_cast<int64_t>(gw) * a.items / a.warps) : 0;
         e = gw < a.warps ? static_cast<int>(static_cast<int64_t>(gw + 1) * a.items / a.warps) : 0;
         per_set = NCOL * a.k_tiles;
-        sb = stage_bytes(a.m);
         smem_base = static_cast<uint32_t>(__cvta_generic_to_shared(g_smem));
-        ring = warp * S * sb;
+        ring = warp * S * kSb;
         // This lane's 16 bytes of weight chunk c are at tile + 512 c + wlane: K rows 16c + 4t .. +3, column group g.
         wlane = 256 * (t >> 1) + 32 * g + 16 * (t & 1);
-        bars = smem_base + W * S * sb + warp * S * 8;
+        bars = smem_base + W * S * kSb + warp * S * 8;
         // x rows of a tile: 16 m copies of 16 bytes, taken by the lanes in turn (copy lane + 32 r).
 #pragma unroll
         for (int r = 0; r < (16 * MAXM + 31) / 32; ++r) {
@@ -348,21 +348,21 @@ struct GemvWarp {
         const int base = (NCOL == 2 && a.col_stride == 1) ? 2 * c.j : c.j;
         return a.packed + tile_index(a.col_tile0 + base + c.s * a.col_stride, 0, a.tiles_k_total, a.tiles_n_total) * kTileBytes;
     }
-    __device__ __forceinline__ uint32_t stage_addr(int use) const { return ring + (use % S) * sb; }
+    __device__ __forceinline__ uint32_t stage_addr(int slot) const { return ring + slot * kSb; }
 
     // The weight tile of the item at `in`, as one bulk copy (lane 0) onto its stage's barrier.
-    __device__ __forceinline__ void issue_w(int use) {
+    __device__ __forceinline__ void issue_w(int slot) {
         if (lane == 0) {
-            const uint32_t bar = bars + 8 * (use % S);
+            const uint32_t bar = bars + 8 * slot;
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // after this warp's reads of the stage
             mbar_expect_tx(bar, kTileBytes);
-            bulk_load(smem_base + stage_addr(use), in_col + static_cast<int64_t>(in.kt) * kTileBytes, kTileBytes, bar);
+            bulk_load(smem_base + stage_addr(slot), in_col + static_cast<int64_t>(in.kt) * kTileBytes, kTileBytes, bar);
         }
     }
     // Rows of x of the item at `in` (cp.async, one commit group per tile), then advance `in`.
-    __device__ __forceinline__ void issue_x(int use) {
+    __device__ __forceinline__ void issue_x(int slot) {
         const uint8_t *xsrc = reinterpret_cast<const uint8_t *>(a.x + in.kt * kTileK);
-        const uint32_t dst = smem_base + stage_addr(use);
+        const uint32_t dst = smem_base + stage_addr(slot);
 #pragma unroll
         for (int r = 0; r < (16 * MAXM + 31) / 32; ++r)
             if (lane + 32 * r < 16 * a.m) cp_async16(dst + x_dst[r], xsrc + x_src[r]);
@@ -378,7 +378,7 @@ struct GemvWarp {
         const Cursor in0 = in;
         const uint8_t *in_col0 = in_col;
         for (int p = 0; p < S - 1 && b + p < e; ++p) {
-            issue_w(use0 + p);
+            issue_w(p);
             advance();
         }
         in = in0;
@@ -387,10 +387,10 @@ struct GemvWarp {
     __device__ __forceinline__ void start() {
 #pragma unroll
         for (int p = 0; p < S - 1; ++p) {
-            if (b + p < e) issue_x(use0 + p);
+            if (b + p < e) issue_x(p);
             cp_async_commit();
         }
-        in_use = use0 + S - 1;
+        in_slot = S - 1;
     }
 
     // Finishes column set j from acc (slot NCOL-1) and gate (slot 0 when NCOL == 2): from registers
@@ -478,21 +478,26 @@ struct GemvWarp {
         zero(acc);
         zero(gate);
         Cursor cur{b / per_set, (b % per_set) / a.k_tiles, b % a.k_tiles};
-        int use = use0;
-        for (int it = b; it < e; ++it, ++use) {
+        int slot = 0;
+        uint32_t phase = 0;
+        for (int it = b; it < e; ++it) {
             cp_async_wait<S - 2>();
-            if (!mbar_wait(bars + 8 * (use % S), (use / S) & 1)) {
+            if (!mbar_wait(bars + 8 * slot, phase)) {
                 if (lane == 0) atomicOr(a.status, 1);
                 break;
             }
             __syncwarp();
             if (it + S - 1 < e) {
-                issue_w(in_use);
-                issue_x(in_use);
-                ++in_use;
+                issue_w(in_slot);
+                issue_x(in_slot);
+                in_slot = in_slot + 1 == S ? 0 : in_slot + 1;
             }
             cp_async_commit();
-            tile_mma<MT, F16>(stage_addr(use), wlane, xrow, g, acc);
+            tile_mma<MT, F16>(stage_addr(slot), wlane, xrow, g, acc);
+            if (++slot == S) {
+                slot = 0;
+                phase ^= 1;
+            }
             const int j0 = cur.j, s0 = cur.s;
             cur.next(a.k_tiles, NCOL);
             const bool set_done = cur.j != j0 || it + 1 == e;
@@ -515,7 +520,7 @@ struct GemvWarp {
             }
         }
         cp_async_wait<0>();
-        return use0 + (e - b);
+        return e - b;
     }
 };
 
@@ -535,8 +540,8 @@ template <int NCOL, int MT, int W, int S, int MAXM, bool F16, int EPI>
 __global__ void __launch_bounds__(W * 32, 1) gemv_kernel(const GemvArgs a) {
     if (static_cast<int>(blockIdx.x * W + (threadIdx.x >> 5)) >= a.warps) return;
     pdl_launch_dependents();
-    init_ring_barriers<W, S>(stage_bytes(a.m));
-    GemvWarp<NCOL, MT, W, S, MAXM, F16, EPI> w(a, 0);
+    init_ring_barriers<W, S>(stage_bytes(MAXM));
+    GemvWarp<NCOL, MT, W, S, MAXM, F16, EPI> w(a);
     // Weights of the first S - 1 items before the previous kernel has finished; everything that
     // kernel may write (x) or read (y, the workspace) only after pdl_wait().
     w.prefetch();
@@ -565,7 +570,7 @@ int launch(const GemvArgs &a, cudaStream_t stream) {
             configured[dev] = true;
         }
     }
-    const cudaError_t e = launch_pdl(kernel, dim3((a.warps + W - 1) / W), dim3(W * 32), W * S * stage_bytes(a.m) + W * S * 8, stream, a);
+    const cudaError_t e = launch_pdl(kernel, dim3((a.warps + W - 1) / W), dim3(W * 32), smem, stream, a);
     if (e != cudaSuccess) {
         set_cuda_error(e);
         return HMB_ERR_CUDA;

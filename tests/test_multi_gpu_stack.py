@@ -91,7 +91,7 @@ def _rank(rank, world, port, out_path):
             res[f"got{m}"] = got[rows].float().cpu().numpy()
             res[f"ref{m}"] = ref[rows].float().cpu().numpy()
             res[f"graph_same{m}"] = np.array(bool(torch.equal(result, got)))
-            mine = got.view(torch.int16).flatten()
+            mine = got.view(torch.int32).flatten()  # NCCL moves no 16-bit integers
             other = mine.clone()
             dist.broadcast(other, src=0)
             res[f"rank_same{m}"] = np.array(bool(torch.equal(mine, other)))
