@@ -421,7 +421,9 @@ int gemm_run(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const vo
     if (y_dtype != x_dtype && !(y_dtype == HMB_FP32 && epilogue == HMB_EPI_STORE)) return HMB_ERR_ARG;
     if (epilogue == HMB_EPI_SWIGLU && layout != HMB_GATE_UP_BLOCKED && layout != HMB_GATE_UP_INTERLEAVED) return HMB_ERR_ARG;
     if (!hmb_w4a16_gemm_supports(m, k, n, epilogue)) return HMB_ERR_UNSUPPORTED;
-    if (epilogue == HMB_EPI_SWIGLU && layout == HMB_GATE_UP_BLOCKED && (n / 2) % (2 * kTileN)) return HMB_ERR_UNSUPPORTED;
+    // Blocked SwiGLU: the CTA-pair tiles take two gate tile columns at a time; the swap-AB kernel one.
+    if (epilogue == HMB_EPI_SWIGLU && layout == HMB_GATE_UP_BLOCKED && (n / 2) % (2 * kTileN) && !skinny_supported(m, k, n))
+        return HMB_ERR_UNSUPPORTED;
     const int64_t out_cols = epilogue == HMB_EPI_SWIGLU ? n / 2 : n;
     if (ldx < k || ldy < out_cols) return HMB_ERR_ARG;
     if (!aligned(packed, 16) || !aligned(x, 16) || !aligned(y, 16) || ldx % 8 || ldy % 8) return HMB_ERR_ALIGN;

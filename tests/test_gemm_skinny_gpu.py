@@ -5,7 +5,8 @@ so it is compared with the oracle under the LEVEL tolerance of the reference's t
 (kernels/gpu/tests/test_gpu_ffn.cpp:35-36, 112). hmb_w4a16_gemm (no workspace) runs it on whole column
 blocks; hmb_w4a16_ffn (with a workspace) cuts the (block, K step) units into equal shares per SM and
 adds the parts of split blocks in a fixed order, which these tests check against the oracle and for
-bit-identical repeats."""
+bit-identical repeats. The shapes cover even and odd numbers of 128-column blocks, and a blocked
+gate/up layout whose gate half is an odd number of 64-channel tiles (which only this kernel takes)."""
 import numpy as np
 import pytest
 import torch
@@ -57,10 +58,11 @@ def test_skinny_gemm_matches_oracle(cuda, oracle, k, n, m):
     assert_close(y.float().cpu().numpy(), y32, LEVEL, f"skinny gemm k={k} n={n} m={m}")
 
 
+@pytest.mark.parametrize("c", [1024, 576])  # 16 and 9 column blocks
 @pytest.mark.parametrize("layout", [0, 1])
 @pytest.mark.parametrize("m", [33, 128])
-def test_skinny_swiglu(cuda, oracle, layout, m):
-    h, c = 2048, 1024
+def test_skinny_swiglu(cuda, oracle, layout, m, c):
+    h = 2048
     p = rand_matrix(oracle, h, 2 * c, seed=70 + layout)
     x = oracle.bf16_bits(np.random.default_rng(71).standard_normal((m, h)))
     _, gu = oracle.gemv(p, h, 2 * c, x)
@@ -69,7 +71,7 @@ def test_skinny_swiglu(cuda, oracle, layout, m):
     ops.w4a16_gemm(act, dev16(x, cuda), torch.from_numpy(p).to(cuda), h, 2 * c, h, 2 * c, 0, 1, layout)
     torch.cuda.synchronize()
     assert device_status(cuda) == 0
-    assert_close(act.float().cpu().numpy(), act_ref, LEVEL, f"skinny swiglu layout={layout} m={m}")
+    assert_close(act.float().cpu().numpy(), act_ref, LEVEL, f"skinny swiglu layout={layout} m={m} c={c}")
 
 
 def test_skinny_leading_block_start_col_fp32_fp16(cuda, oracle):
