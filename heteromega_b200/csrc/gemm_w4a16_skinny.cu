@@ -27,8 +27,9 @@
 // cycles after its TMA and the ring holds 8 steps, which sets a step to about 750 cycles; the MMA
 // thread needs about 320 cycles to issue a step's 4 MMAs and commit, and a dequant warp about 630.
 // The x tile is re-read from L2 by every SM for each of its blocks (at 64 rows about twice the weight
-// bytes). A variant that fed up to four blocks from one x tile cut that stream by four but the launch
-// only by 15%: the pace is set by the latency of the dequant warps' chains and of MMA issue, not HBM.
+// bytes). Variants that cut that stream (up to four blocks per x tile, or CTA pairs that each stage half
+// of every x tile and share M = 256 MMAs) were at most 15% faster per launch: neither the x stream nor
+// MMA issue, and not HBM, sets the pace, but the latency of each step's chain from packed tile to MMA.
 //
 // Roles in a CTA of 15 warps:
 //   warp 0      TMA of the x tile [nt tokens x 64] of each step;
