@@ -15,6 +15,7 @@ HMB_ERR_ARG, HMB_ERR_ALIGN, HMB_ERR_VALUE, HMB_ERR_WORKSPACE, HMB_ERR_UNSUPPORTE
 HMB_BF16, HMB_FP16, HMB_FP32 = 0, 1, 2
 HMB_GATE_UP_BLOCKED, HMB_GATE_UP_INTERLEAVED = 0, 1
 HMB_EPI_STORE, HMB_EPI_SWIGLU = 0, 1
+HMB_TP_CHAIN_IN, HMB_TP_CHAIN_OUT = 1, 2
 TILE_K, TILE_N, TILE_BYTES = 128, 64, 4352
 
 _i64 = ctypes.c_int64
@@ -56,6 +57,8 @@ SIGNATURES = {
     "hmb_tp_ffn_layer": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp, _vp, _vp, ctypes.c_float, _i64, _vp, _sz, _vp,
                                 ctypes.c_uint64]),
     "hmb_tp_ffn_layer_workspace": (_sz, [_i64, _i64, _i64]),
+    "hmb_tp_ffn_layer_chained": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _int, _vp, _vp, _vp, ctypes.c_float, _i64, _vp, _sz,
+                                        _vp, ctypes.c_uint64, _int]),
     "hmb_comm_rows": (_int, [_vp, _i64, _i64, _vp, _vp]),
     "hmb_device_status": (_int, [_vp, _vp]),
     "hmb_silu_mul": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _int, _vp]),

@@ -27,6 +27,10 @@
 //     c stores the rounded sum into every rank's gather slot; each rank copies the chunks into y.
 // The boundary kernel cuts by rows instead (a row needs all its values for the norm): rank c owns
 // rows [c*m/P, (c+1)*m/P). Its CTAs process whole rows, so they wait for the flags of every CTA.
+// Chained (two-shot): instead of waiting at its end until every rank's rows have arrived, each CTA
+// counts the rows it stored into row-block counters (256 rows a block) on every rank and leaves; the
+// next layer's gate/up GEMM waits per row block on this rank's counters before it loads x, so the
+// gather overlaps that GEMM. A chained call zeroes this rank's counters before its first flags.
 // Every wait gives up after spin_limit_ns (default one second) and ORs 1 into the device status word.
 #include <cuda.h>
 
@@ -47,6 +51,8 @@ constexpr int kCtas = 128;
 constexpr int kThreads = 256;    // 16 bytes each: one 4 KB block per pass
 constexpr int64_t kBlock = 4096;
 constexpr size_t kFlagBytes = 2 * 2 * kMaxRanks * kCtas * 4;  // [phase][parity][rank][cta]
+constexpr int64_t kReadyBlocks = 4096;                         // row-block counters of a chained boundary
+constexpr size_t kHeadBytes = kFlagBytes + kReadyBlocks * 4;   // flags and counters, then the slots
 constexpr int64_t kOneShotBytes = 512 * 1024;
 constexpr size_t kRowSlack = 2 * kRowMaxH;  // a row-cut chunk can exceed 1/P of a message by one row
 static_assert(kThreads == kRowThreads, "the boundary kernel processes rows with the whole CTA");
@@ -84,10 +90,14 @@ struct BnArgs {
     int two_shot;
     int prefilled;       // the partials are already in the slots (a scatter wrote them); y unused
     int64_t out_offset;  // of the output region in every symmetric buffer
+    int chained;         // two-shot: count rows into the ready counters instead of waiting for them
 };
 
 __device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void red_release_sys(unsigned *p, unsigned v) {
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
     unsigned v;
@@ -106,7 +116,11 @@ __device__ __forceinline__ unsigned *flag(const Link &l, int owner, int phase, i
 }
 // Receive slot (phase 0: reduce-scatter / one-shot, phase 1: gather) for data from rank `from`.
 __device__ __forceinline__ uint8_t *slot(const Link &l, int owner, int phase, int parity, int from) {
-    return l.p.base[owner] + kFlagBytes + ((static_cast<int64_t>(phase) * 2 + parity) * l.world + from) * l.slot_bytes;
+    return l.p.base[owner] + kHeadBytes + ((static_cast<int64_t>(phase) * 2 + parity) * l.world + from) * l.slot_bytes;
+}
+// Row-block counter mb of a chained boundary in the buffer of rank `owner`.
+__device__ __forceinline__ unsigned *ready(const Link &l, int owner, int64_t mb) {
+    return reinterpret_cast<unsigned *>(l.p.base[owner] + kFlagBytes) + mb;
 }
 
 // Spins (bounded) until the flag reaches `epoch`.
@@ -319,6 +333,12 @@ __global__ void __launch_bounds__(kThreads, 1) boundary_kernel(const BnArgs a) {
         return;
     }
 
+    // Chained: this rank's counters start from zero; the flags below publish that before any rank
+    // counts rows of this call into them (the previous call's counts were consumed by the GEMM that
+    // ran before this kernel).
+    if (a.chained)
+        for (int64_t mb = blockIdx.x * kThreads + threadIdx.x; mb < (a.m + 255) / 256; mb += kCtas * kThreads)
+            *ready(l, l.rank, mb) = 0u;
     // Reduce-scatter by rows: rank c's rows of this rank's partial into rank c's slot[me].
     if (!a.prefilled)
         for (int j = 1; j < l.world; ++j) {  // owners visited from the next rank on: no incast
@@ -334,9 +354,31 @@ __global__ void __launch_bounds__(kThreads, 1) boundary_kernel(const BnArgs a) {
         for (int r = 0; r < NW; ++r) {
             in[r] = r == l.rank && own_y ? ya + row * a.h
                                          : reinterpret_cast<const AT *>(slot(l, l.rank, 0, par, r) + (row - r0) * row_bytes);
-            out[r] = reinterpret_cast<uint16_t *>(l.p.base[r] + a.out_offset) + row * a.h;
+            // Destinations from this rank on, so the ranks do not all store into one GPU at once.
+            const int d = (l.rank + r) % NW;
+            out[r] = reinterpret_cast<uint16_t *>(l.p.base[d] + a.out_offset) + row * a.h;
         }
         boundary_row<V, NW, AT>(in, a.x + row * a.h, true, a.w, a.h, a.eps, out, NW, red);
+    }
+    if (a.chained) {
+        // Count this CTA's rows into every rank's row-block counters, after its stores: the CTA
+        // barrier, then a release at system scope by the counting threads (one per rank).
+        __syncthreads();
+        if (threadIdx.x < NW) {
+            const int d = (l.rank + threadIdx.x) % NW;
+            int64_t mb = -1;
+            unsigned n = 0;
+            for (int64_t row = r0 + blockIdx.x; row < r1; row += kCtas) {
+                if (row / 256 != mb) {
+                    if (n) red_release_sys(ready(l, d, mb), n);
+                    mb = row / 256;
+                    n = 0;
+                }
+                ++n;
+            }
+            if (n) red_release_sys(ready(l, d, mb), n);
+        }
+        return;
     }
     // The kernel ends only when every rank's rows have arrived in this rank's output region.
     raise_flags(l, 1, par, epoch);
@@ -406,6 +448,14 @@ namespace hmb {
 
 int comm_world(const hmb_comm *c) { return c ? c->world : 0; }
 
+bool comm_chains(const hmb_comm *c, int64_t m, int64_t h) {
+    return c && c->connected && c->world > 1 && m * h * 2 > kOneShotBytes && (m + 255) / 256 <= kReadyBlocks;
+}
+
+const unsigned *comm_ready(const hmb_comm *c) { return c ? reinterpret_cast<const unsigned *>(c->mine + kFlagBytes) : nullptr; }
+
+const void *comm_out_region(const hmb_comm *c) { return c ? c->mine + c->out_offset : nullptr; }
+
 int comm_scatter_target(const hmb_comm *c, int64_t m, int64_t h, ScatterTarget *t) {
     if (!c || !t || m <= 0 || h <= 0 || h % 8) return HMB_ERR_ARG;
     if (!c->connected) return HMB_ERR_ARG;
@@ -415,7 +465,7 @@ int comm_scatter_target(const hmb_comm *c, int64_t m, int64_t h, ScatterTarget *
     if (!all && static_cast<size_t>((comm_share_row(m, c->world, 1) + 1) * 2 * h) > c->slot_bytes) return HMB_ERR_WORKSPACE;
     *t = ScatterTarget{};
     for (int r = 0; r < c->world; ++r) t->base[r] = c->peers.base[r];
-    t->slot0 = static_cast<int64_t>(kFlagBytes);
+    t->slot0 = static_cast<int64_t>(kHeadBytes);
     t->slot_bytes = static_cast<int64_t>(c->slot_bytes);
     t->world = c->world;
     t->rank = c->rank;
@@ -427,7 +477,7 @@ int comm_scatter_target(const hmb_comm *c, int64_t m, int64_t h, ScatterTarget *
 }
 
 int comm_boundary(hmb_comm *c, const void *y, int y_dtype, void *x, const void *weight, int64_t m, int64_t h, float eps,
-                  bool prefilled, cudaStream_t s, uint64_t spin_limit_ns) {
+                  bool prefilled, cudaStream_t s, uint64_t spin_limit_ns, bool chained) {
     if (!x || !c || m <= 0 || h <= 0 || h % 8 || h > kRowMaxH || !(eps >= 0.0f)) return HMB_ERR_ARG;
     if (!c->connected || (!y && !prefilled)) return HMB_ERR_ARG;
     if (y_dtype != HMB_BF16 && y_dtype != HMB_FP32) return HMB_ERR_ARG;
@@ -455,6 +505,7 @@ int comm_boundary(hmb_comm *c, const void *y, int y_dtype, void *x, const void *
     a.two_shot = two_shot;
     a.prefilled = prefilled;
     a.out_offset = static_cast<int64_t>(c->out_offset);
+    a.chained = chained && comm_chains(c, m, h);
     const cudaError_t e = launch_boundary(row_vectors(h), c->world, y_dtype == HMB_FP32, s, a);
     if (e != cudaSuccess) {
         set_cuda_error(e);
@@ -480,10 +531,10 @@ int hmb_comm_create(int rank, int world, size_t max_bytes, hmb_comm **out, void 
     // partials), a two-shot slot one chunk of it (for the boundary, one rank's rows: at most one row
     // more than 1/P of the message).
     c->slot_bytes = std::max<size_t>(2 * kOneShotBytes, ((c->max_bytes + world - 1) / world + kRowSlack + 255) / 256 * 256);
-    c->out_offset = kFlagBytes + 2 * 2 * static_cast<size_t>(world) * c->slot_bytes;
+    c->out_offset = kHeadBytes + 2 * 2 * static_cast<size_t>(world) * c->slot_bytes;
     const size_t bytes = c->out_offset + c->max_bytes;
     cudaError_t e = cudaMalloc(&c->mine, bytes);
-    if (e == cudaSuccess) e = cudaMemset(c->mine, 0, kFlagBytes);
+    if (e == cudaSuccess) e = cudaMemset(c->mine, 0, kHeadBytes);
     if (e == cudaSuccess) e = cudaMalloc(&c->epochs, kCtas * sizeof(unsigned));
     if (e == cudaSuccess) e = cudaMemset(c->epochs, 0, kCtas * sizeof(unsigned));
     cudaIpcMemHandle_t h;

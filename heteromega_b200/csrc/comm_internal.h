@@ -53,8 +53,17 @@ int comm_world(const hmb_comm *c);
 int comm_scatter_target(const hmb_comm *c, int64_t m, int64_t h, ScatterTarget *t);
 
 // hmb_allreduce_residual_norm; with `prefilled` the partials are already in the slots (written by
-// a scatter to comm_scatter_target, bf16) and y is not read.
+// a scatter to comm_scatter_target, bf16) and y is not read. `chained` (taken where comm_chains):
+// the call ends once this rank's rows are stored, and every rank's row-block counters (comm_ready)
+// count the rows as they land; the next reader of the output region waits on them.
 int comm_boundary(hmb_comm *c, const void *y, int y_dtype, void *x, const void *weight, int64_t m, int64_t h, float eps,
-                  bool prefilled, cudaStream_t stream, uint64_t spin_limit_ns);
+                  bool prefilled, cudaStream_t stream, uint64_t spin_limit_ns, bool chained = false);
+
+// Whether an m x h boundary on this communicator can be chained (two-shot, two or more ranks).
+bool comm_chains(const hmb_comm *c, int64_t m, int64_t h);
+// This rank's row-block counters (row block mb = rows [256 mb, 256 mb + 256) of the output region
+// holds all its rows once counter mb = min(256, m - 256 mb)) and the output region itself.
+const unsigned *comm_ready(const hmb_comm *c);
+const void *comm_out_region(const hmb_comm *c);
 
 }  // namespace hmb

@@ -32,6 +32,8 @@ struct PairArgs {
     unsigned *split_cnt;  // k_splits > 1: [tile][CTA] arrival and completion counters (self-resetting)
     int scatter;          // HMB_EPI_STORE, 16-bit output: rows go to the communicator's receive slots `sc`
     ScatterTarget sc;
+    const unsigned *x_ready;  // non-null: row block mb of x is complete once x_ready[mb] = min(256, m - 256 mb)
+    int mb_rot;               // row blocks visited from this one on (a rank's own rows first)
 };
 
 // The band order of an m x k x n problem (m_blocks x n_blocks tiles of 256 x 256): the direction
@@ -91,9 +93,12 @@ GemmPlan gemm_plan(int64_t m, int64_t k, int64_t n, bool split_ws, bool scatter)
 // zero). Without them (nullptr) no K splits are used. With a scatter target (HMB_EPI_STORE, 16-bit
 // output, n == sc->h, m == sc->m) the output rows go to a communicator's receive slots instead of y,
 // always through the CTA-pair kernel.
+// x_ready / x_rot (the CTA-pair kernel only, ignored by the others): wait per row block of x on the
+// counters of a chained boundary before loading it, and start at row block x_rot.
 int gemm_run(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const void *x, int64_t ldx, int x_dtype, void *y, int64_t ldy,
              int y_dtype, int64_t m, int64_t k, int64_t n, int64_t start_col, int epilogue, int layout, void *split_ws, size_t split_ws_bytes,
-             unsigned *split_cnt, cudaStream_t stream, const ScatterTarget *sc = nullptr);
+             unsigned *split_cnt, cudaStream_t stream, const ScatterTarget *sc = nullptr, const unsigned *x_ready = nullptr,
+             int x_rot = 0);
 constexpr size_t kSplitCounterBytes = 4096;
 
 // Launches the CTA-pair kernel; `map` is x as a 2D tensor map with 64 x 128 boxes (SWIZZLE_128B).

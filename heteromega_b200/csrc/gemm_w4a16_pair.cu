@@ -229,10 +229,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // stays in L2 while the column blocks of the weights stream past it, row blocks fastest inside
     // the band; or the mirror image with a band of column blocks. The pairs working at one time hold
     // consecutive tiles, so each weight (or x) block comes from DRAM about once per band.
-    // Scattering to row owners, every rank starts its row blocks at its own offset (rank * m_blocks
-    // / P): at any moment rank r stores to a different owner than the other ranks, instead of all
-    // ranks pouring their rows into the same one or two GPUs.
-    const int mb_shift = a.scatter && !a.sc.all ? static_cast<int>(static_cast<int64_t>(a.sc.rank) * a.m_blocks / a.sc.world) : 0;
+    // Row blocks from a.mb_rot on. Scattering to row owners, every rank starts at its own offset
+    // (rank * m_blocks / P): at any moment rank r stores to a different owner than the other ranks,
+    // instead of all ranks pouring their rows into the same one or two GPUs. Reading x from a chained
+    // boundary, a rank starts at its own rows, which it stored itself.
+    const int mb_shift = a.mb_rot;
     auto tile_mb = [&](int t) {
         const int per = a.band * (a.band_rows ? a.n_blocks : a.m_blocks), b = t / per, i = t - b * per;
         const int g = min(a.band, (a.band_rows ? a.m_blocks : a.n_blocks) - b * a.band);
@@ -293,6 +294,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int unit = cluster; ok && unit < num_units; unit += nclusters) {
                 const int mb = tile_mb(unit / a.k_splits);
                 const int row0 = 256 * mb + 128 * static_cast<int>(rank);
+                // x from a chained boundary: the row block's rows have all landed (bounded wait), then
+                // the TMA (async proxy) reads what the peers stored.
+                if (a.x_ready && !wait_rows(a.x_ready + mb, static_cast<unsigned>(min(256, a.m - 256 * mb)), abort, a.status)) break;
                 for (int i = unit_k0(unit); i < unit_k1(unit); ++i, ++it) {
                     const int s = it % kXStages, u = it / kXStages;
                     if (u > 0 && !mbar_wait(done(s), (u - 1) & 1, abort, a.status)) {

@@ -406,7 +406,7 @@ GemmPlan gemm_plan(int64_t m, int64_t k, int64_t n, bool split_ws, bool scatter)
 
 int gemm_run(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const void *x, int64_t ldx, int x_dtype, void *y, int64_t ldy,
              int y_dtype, int64_t m, int64_t k, int64_t n, int64_t start_col, int epilogue, int layout, void *split_ws, size_t split_ws_bytes,
-             unsigned *split_cnt, cudaStream_t stream, const ScatterTarget *sc) {
+             unsigned *split_cnt, cudaStream_t stream, const ScatterTarget *sc, const unsigned *x_ready, int x_rot) {
     if (!packed || !x || (!y && !sc) || m <= 0) return HMB_ERR_ARG;
     if (sc && (epilogue != HMB_EPI_STORE || y_dtype == HMB_FP32 || sc->h != n || sc->m != m)) return HMB_ERR_ARG;
     if (sc) {
@@ -503,7 +503,12 @@ int gemm_run(const uint8_t *packed, int64_t packed_k, int64_t packed_n, const vo
         if (sc) {
             p.scatter = 1;
             p.sc = *sc;
+            // Scattering to row owners, every rank starts its row blocks at its own offset: at any
+            // moment rank r stores to a different owner than the other ranks.
+            if (!sc->all) p.mb_rot = static_cast<int>(static_cast<int64_t>(sc->rank) * p.m_blocks / sc->world);
         }
+        p.x_ready = x_ready;
+        if (x_ready) p.mb_rot = ((x_rot % p.m_blocks) + p.m_blocks) % p.m_blocks;
         return launch_gemm_pair(map, p, f16, epilogue, stream);
     }
     GemmArgs a{};

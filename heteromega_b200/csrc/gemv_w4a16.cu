@@ -781,6 +781,13 @@ size_t hmb_tp_ffn_layer_workspace(int64_t m, int64_t h, int64_t n) {
 int hmb_tp_ffn_layer(hmb_comm *comm, const uint8_t *gate_up, const uint8_t *down, int64_t h, int64_t n, int64_t stored, int layout,
                      const void *x, void *resid, const void *norm_weight, float eps, int64_t m, void *workspace, size_t workspace_bytes,
                      hmb_stream_t stream, uint64_t spin_limit_ns) {
+    return hmb_tp_ffn_layer_chained(comm, gate_up, down, h, n, stored, layout, x, resid, norm_weight, eps, m, workspace, workspace_bytes,
+                                    stream, spin_limit_ns, 0);
+}
+
+int hmb_tp_ffn_layer_chained(hmb_comm *comm, const uint8_t *gate_up, const uint8_t *down, int64_t h, int64_t n, int64_t stored,
+                             int layout, const void *x, void *resid, const void *norm_weight, float eps, int64_t m, void *workspace,
+                             size_t workspace_bytes, hmb_stream_t stream, uint64_t spin_limit_ns, int chain) {
     if (!comm || !gate_up || !down || !x || !resid || m <= 0) return HMB_ERR_ARG;
     const size_t ffn_bytes = hmb_w4a16_ffn_workspace(m, h, n);
     if (!ffn_bytes) return HMB_ERR_ARG;
@@ -796,22 +803,30 @@ int hmb_tp_ffn_layer(hmb_comm *comm, const uint8_t *gate_up, const uint8_t *down
     const bool same_up = layout == HMB_GATE_UP_INTERLEAVED || n == stored;
     const bool fused = m > 16 && same_up && hmb_w4a16_gemm_supports(m, h, 2 * n, HMB_EPI_SWIGLU) &&
                        hmb_w4a16_gemm_supports(m, n, h, HMB_EPI_STORE) && comm_scatter_target(comm, m, h, &t) == HMB_OK && t.world > 1;
+    if (chain & ~(HMB_TP_CHAIN_IN | HMB_TP_CHAIN_OUT)) return HMB_ERR_ARG;
     if (fused) {
         if (h % kTileK || n % kTileK || stored % kTileK || n > stored) return HMB_ERR_ARG;
         if (layout != HMB_GATE_UP_BLOCKED && layout != HMB_GATE_UP_INTERLEAVED) return HMB_ERR_ARG;
         if (!aligned(x, 16)) return HMB_ERR_ALIGN;
+        // Chaining (two-shot boundaries read by the CTA-pair gate/up GEMM): the same condition in
+        // consecutive calls of one stack, so a chained boundary's counters meet a waiting GEMM.
+        const bool chain_ok = comm_chains(comm, m, h) && gemm_plan(m, h, 2 * n, false, false).pair;
+        const bool chain_in = chain_ok && (chain & HMB_TP_CHAIN_IN), chain_out = chain_ok && (chain & HMB_TP_CHAIN_OUT);
+        if (chain_in && x != comm_out_region(comm)) return HMB_ERR_ARG;
         unsigned *gu_split_cnt = reinterpret_cast<unsigned *>(ws + 2 * kCounterBytes);
         unsigned *dn_split_cnt = reinterpret_cast<unsigned *>(ws + 2 * kCounterBytes + kSplitCounterBytes);
         uint8_t *act_p = ws + kFfnControlBytes;
         uint8_t *scratch = act_p + round256(static_cast<size_t>(m) * n * 2);
         const size_t scratch_bytes = ffn_bytes - (scratch - ws);
+        // Chained in: the rows of x land while this GEMM runs; it starts at this rank's own rows.
+        const int own_block = static_cast<int>(comm_share_row(m, t.world, t.rank) / 256);
         int rc = gemm_run(gate_up, h, 2 * stored, x, h, HMB_BF16, act_p, n, HMB_BF16, m, h, 2 * n, 0, HMB_EPI_SWIGLU, layout, scratch,
-                          scratch_bytes, gu_split_cnt, s);
+                          scratch_bytes, gu_split_cnt, s, nullptr, chain_in ? comm_ready(comm) : nullptr, own_block);
         if (rc != HMB_OK) return rc;
         rc = gemm_run(down, stored, h, act_p, n, HMB_BF16, nullptr, h, HMB_BF16, m, n, h, 0, HMB_EPI_STORE, 0, scratch, scratch_bytes,
                       dn_split_cnt, s, &t);
         if (rc != HMB_OK) return rc;
-        return comm_boundary(comm, nullptr, HMB_BF16, resid, norm_weight, m, h, eps, true, s, spin_limit_ns);
+        return comm_boundary(comm, nullptr, HMB_BF16, resid, norm_weight, m, h, eps, true, s, spin_limit_ns, chain_out);
     }
     // Decode (and a group of one): the FFN into y, then the boundary with its own exchange. Across
     // ranks the partials stay fp32 (unrounded sums): the messages are small, and P rounded partials

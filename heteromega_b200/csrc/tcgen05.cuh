@@ -90,6 +90,33 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
 }
 
+// Spins (bounded like mbar_wait) until the counter at p reaches `need` (acquire at system scope: it is
+// raised by other GPUs after their stores), then orders this thread's later bulk-tensor copies, which
+// read through the async proxy, after what it acquired.
+__device__ __forceinline__ bool wait_rows(const unsigned *p, unsigned need, volatile int *abort, int *status) {
+    uint64_t start = 0;
+    for (uint32_t i = 0;; ++i) {
+        unsigned v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+        if (v >= need) {
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            return true;
+        }
+        if ((i & 15) == 15) {
+            if (*abort) return false;
+            const uint64_t now = global_ns();
+            if (start == 0) {
+                start = now;
+            } else if (now - start > kWaitLimitNs) {
+                *abort = 1;
+                atomicOr(status, 1);
+                return false;
+            }
+        }
+        __nanosleep(64);
+    }
+}
+
 // 2D TMA tile load into this CTA's shared memory, completing on a barrier of this CTA.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
     asm volatile(

@@ -36,6 +36,7 @@ class FfnStack:
             raise ValueError("FfnStack: one norm weight per layer")
         self.norms = [n.to(self.device, torch.bfloat16).contiguous() for n in norms]
         self.eps = float(eps)
+        self.chain = False  # tensor parallel: overlap each boundary's gather with the next gate/up GEMM
         self._graphs = {}
         self._copy_streams = None
 
@@ -63,7 +64,8 @@ class FfnStack:
             last = l == L - 1
             g = None if last else self.norms[l + 1]
             if fused:
-                out = self.tp.layer(l, x, h, g, self.eps)
+                # Chained boundaries: each layer's gather completes under the next layer's gate/up GEMM.
+                out = self.tp.layer(l, x, h, g, self.eps, chain_in=self.chain and l > 0, chain_out=self.chain and not last)
             elif self.tp is None:
                 w: FfnSliceWeights = self.layers[l]
                 ops.w4a16_ffn(y, x, w.gate_up, w.down, w.hidden, w.channels(), w.stored_channels(), int(w.layout))

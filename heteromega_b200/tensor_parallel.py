@@ -191,11 +191,14 @@ class TensorParallelFfn:
         ops.residual_norm(h, partial, None, weight, normed, eps)
         return normed
 
-    def layer(self, layer, x, h, weight, eps, spin_limit_ns=0):
-        """One whole layer with its boundary on the NVLink communicator (hmb_tp_ffn_layer): this rank's
-        partial of FFN `layer` for x [m, H], summed over the ranks into h's kept rows, and the next
-        input RMSNorm(h) * weight (h itself without weight) in the output region, whose view it
-        returns. For m > 16 the down GEMM writes its partial rows straight into the peers' slots."""
+    def layer(self, layer, x, h, weight, eps, spin_limit_ns=0, chain_in=False, chain_out=False):
+        """One whole layer with its boundary on the NVLink communicator (hmb_tp_ffn_layer_chained): this
+        rank's partial of FFN `layer` for x [m, H], summed over the ranks into h's kept rows, and the
+        next input RMSNorm(h) * weight (h itself without weight) in the output region, whose view it
+        returns. For m > 16 the down GEMM writes its partial rows straight into the peers' slots.
+        chain_out: the boundary leaves the gather to complete under the next call, which must be made
+        with chain_in (x = this call's output region) before anything else reads the region; its
+        gate/up GEMM then waits per row block for the rows to land (same bits as unchained calls)."""
         if self.comm is None:
             raise RuntimeError("TensorParallelFfn: call connect(max_rows, device) on every rank first")
         w = self.layers[layer]
@@ -205,11 +208,12 @@ class TensorParallelFfn:
                 raise ValueError(f"TensorParallelFfn.layer: {name} must be contiguous bf16 [m, hidden]")
         nbytes = lib().hmb_tp_ffn_layer_workspace(m, w.hidden, w.channels())
         ws = workspace(h.device, nbytes, kind="tp_layer")
-        check(lib().hmb_tp_ffn_layer(self.comm._ptr, w.gate_up.data_ptr(), w.down.data_ptr(), w.hidden, w.channels(),
-                                     w.stored_channels(), int(w.layout), x.data_ptr(), h.data_ptr(),
-                                     weight.data_ptr() if weight is not None else None, float(eps), m, ws.data_ptr(),
-                                     ws.numel(), torch.cuda.current_stream(h.device).cuda_stream, spin_limit_ns),
-              "hmb_tp_ffn_layer")
+        chain = (_lib.HMB_TP_CHAIN_IN if chain_in else 0) | (_lib.HMB_TP_CHAIN_OUT if chain_out else 0)
+        check(lib().hmb_tp_ffn_layer_chained(self.comm._ptr, w.gate_up.data_ptr(), w.down.data_ptr(), w.hidden, w.channels(),
+                                             w.stored_channels(), int(w.layout), x.data_ptr(), h.data_ptr(),
+                                             weight.data_ptr() if weight is not None else None, float(eps), m, ws.data_ptr(),
+                                             ws.numel(), torch.cuda.current_stream(h.device).cuda_stream, spin_limit_ns, chain),
+              "hmb_tp_ffn_layer_chained")
         return self.comm.out(m, self.hidden)
 
     def forward(self, layer, x, y):

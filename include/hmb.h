@@ -243,6 +243,21 @@ int hmb_tp_ffn_layer(hmb_comm *comm, const uint8_t *gate_up, const uint8_t *down
                      const void *x, void *resid, const void *norm_weight, float eps, int64_t m, void *workspace, size_t workspace_bytes,
                      hmb_stream_t stream, uint64_t spin_limit_ns);
 size_t hmb_tp_ffn_layer_workspace(int64_t m, int64_t h, int64_t n);
+/* hmb_tp_ffn_layer for the layers of a stack, overlapping each boundary's gather with the next layer's
+ * gate/up GEMM (no reference counterpart: the reference has no tensor parallelism). chain is a set of
+ * HMB_TP_CHAIN_* bits, taken where the boundary is two-shot and gate/up runs on CTA pairs (m > 128):
+ *   HMB_TP_CHAIN_OUT  the boundary returns once this rank's rows are stored; the output region is
+ *                     complete only for a following HMB_TP_CHAIN_IN call on the same communicator, which
+ *                     must come next (same m, h, n), before anything else reads the region;
+ *   HMB_TP_CHAIN_IN   x is the output region of the previous call, made with HMB_TP_CHAIN_OUT: the gate/up
+ *                     GEMM waits per 256-row block until its rows have landed, starting at this rank's
+ *                     own rows.
+ * The results are the same bits as unchained calls. Any other bit is HMB_ERR_ARG. */
+#define HMB_TP_CHAIN_IN 1
+#define HMB_TP_CHAIN_OUT 2
+int hmb_tp_ffn_layer_chained(hmb_comm *comm, const uint8_t *gate_up, const uint8_t *down, int64_t h, int64_t n, int64_t stored,
+                             int layout, const void *x, void *resid, const void *norm_weight, float eps, int64_t m, void *workspace,
+                             size_t workspace_bytes, hmb_stream_t stream, uint64_t spin_limit_ns, int chain);
 /* The output region of hmb_allreduce_residual_norm: *ptr (256-byte aligned), *bytes = max_bytes. */
 int hmb_comm_out(hmb_comm *comm, void **ptr, size_t *bytes);
 /* Rows [*begin, *end) of an m x h boundary whose residual this rank keeps (all rows when one-shot). */

@@ -8,7 +8,8 @@ same two whole layers run on one GPU as the reference. Checked, on every rank:
     reference's tests (kernels/gpu/tests/test_gpu_ffn.cpp:35-36), at M = 1 and 16 (decode: fp32 partials
     exchanged by the boundary) and M = 8192 (prefill: the down GEMM scatters bf16 partial rows into the
     owners' receive slots);
-  * the same output bits on every rank, and on a graph replay;
+  * the same output bits on every rank, on a graph replay, and with the boundaries unchained (each
+    gather completed inside its boundary instead of under the next layer's gate/up GEMM);
   * the fused layer against the unfused one (local partial, then the exchanging boundary), bit for bit;
   * a clear device status word.
 The rank sum replaces the reference's two-device boundary sum (src/unified_llm_w4a16_hetero/merged_ffn.cpp:417,
@@ -91,6 +92,14 @@ def _rank(rank, world, port, out_path):
             res[f"got{m}"] = got[rows].float().cpu().numpy()
             res[f"ref{m}"] = ref[rows].float().cpu().numpy()
             res[f"graph_same{m}"] = np.array(bool(torch.equal(result, got)))
+            # Chained boundaries (each gather completing under the next gate/up GEMM) against unchained
+            # layers: the same bits.
+            st_tp.chain = False
+            unchained = torch.empty_like(h0)
+            st_tp.forward(h0, unchained)
+            st_tp.chain = True
+            torch.cuda.synchronize()
+            res[f"chain_same{m}"] = np.array(bool(torch.equal(unchained, got)))
             mine = got.view(torch.int32).flatten()  # NCCL moves no 16-bit integers
             other = mine.clone()
             dist.broadcast(other, src=0)
@@ -139,6 +148,7 @@ def test_all_gpus_llama70b_stack(tmp_path):
         for m in MS:
             assert bool(r[f"rank_same{m}"]), f"rank {rank} M={m}: output bits differ from rank 0"
             assert bool(r[f"graph_same{m}"]), f"rank {rank} M={m}: graph replay differs"
+            assert bool(r[f"chain_same{m}"]), f"rank {rank} M={m}: chained boundaries differ from unchained layers"
             max_rel, rel_l2, cos = compare(r[f"got{m}"], r[f"ref{m}"])
             summary.append((rank, m, max_rel, rel_l2, cos))
             assert max_rel <= LEVEL[0] and rel_l2 <= LEVEL[1] and cos >= LEVEL[2], \
