@@ -80,6 +80,8 @@ def parse():
     ap.add_argument("--impl", default="hmb", choices=["hmb", "reference"])
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--cpu-sample-s", type=float, default=10.0)
+    ap.add_argument("--micro", default="", choices=["", "small", "small-once"],
+                    help="instead of the stack: time the small kernels at 70B sizes (small-once: one launch each)")
     return ap.parse_args()
 
 
@@ -729,8 +731,71 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_small(once):
+    """The small kernels at Llama-3-70B sizes on cuda:0, inputs above L2: SiLU*up of [4096, 2 x 28672],
+    the boundary sums of [4096, 8192] (residual_add2, residual_norm), and the packed-matrix kernels on
+    K = 4096 x N = 28672 (dequant to fp32, a full reversed tile gather, the device packer). Each is timed
+    with CUDA events over 5 launches after one warm-up; prints one JSON line of microseconds and
+    algorithmic GB/s per kernel. `once`: one launch each and no timing (for a profiler's launch list)."""
+    import torch
+
+    from heteromega_b200 import _lib
+    from heteromega_b200.torch_ops import ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    m, h, inter, k, n = 4096, 8192, 28672, 4096, 28672
+    res = {}
+
+    def timed(name, fn, nbytes, reps=5):
+        fn()
+        torch.cuda.synchronize()
+        if once:
+            return
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(reps):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        t = s.elapsed_time(e) / reps
+        res[name] = {"us": round(t * 1000, 1), "gbs": round(nbytes / t / 1e6, 1), "bytes": nbytes}
+
+    gu = torch.randn(m, 2 * inter, device=dev, generator=g).to(torch.bfloat16)
+    act = torch.empty(m, inter, dtype=torch.bfloat16, device=dev)
+    timed("silu_mul", lambda: ops.silu_mul(gu, act, _lib.HMB_GATE_UP_INTERLEAVED), (gu.numel() + act.numel()) * 2)
+    del gu, act
+    x, a, b = (torch.randn(m, h, device=dev, generator=g).to(torch.bfloat16) for _ in range(3))
+    w = torch.ones(h, dtype=torch.bfloat16, device=dev)
+    normed = torch.empty_like(x)
+    timed("residual_add2", lambda: ops.residual_add2(x, a, b), 4 * x.numel() * 2)
+    timed("residual_norm", lambda: ops.residual_norm(x, a, b, w, normed, 1e-5), 5 * x.numel() * 2)
+    del x, a, b, normed
+    tiles = (k // 128) * (n // 64)
+    packed = torch.randint(0, 256, (tiles * 4352,), dtype=torch.uint8, device=dev, generator=g)
+    out = torch.empty(k, n, dtype=torch.float32, device=dev)
+    timed("w4a16_dequant", lambda: ops.w4a16_dequant(out, packed, k, n, k, n), packed.numel() + out.numel() * 4)
+    del out
+    idx = torch.arange(tiles - 1, -1, -1, dtype=torch.int64, device=dev)
+    dst = torch.empty_like(packed)
+    timed("gather_tiles", lambda: ops.gather_tiles(dst, packed, packed, idx), 2 * packed.numel())
+    del dst
+    q = torch.randint(0, 16, (k, n), dtype=torch.uint8, device=dev, generator=g)
+    sc = torch.rand(k // 128, n, device=dev, generator=g).to(torch.bfloat16).view(torch.int16)
+    zr = torch.randint(0, 16, (k // 128, n), dtype=torch.uint8, device=dev, generator=g)
+    bad = torch.zeros(1, dtype=torch.int32, device=dev)
+    timed("pack_w4a16_device", lambda: ops.pack_w4a16_device(packed, q, sc, zr, bad),
+          q.numel() + sc.numel() * 2 + zr.numel() + packed.numel())
+    print(json.dumps({"micro": "small", "once": once, "kernels": res}), flush=True)
+
+
 def main():
     args = parse()
+    if args.micro:
+        run_small(args.micro == "small-once")
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
