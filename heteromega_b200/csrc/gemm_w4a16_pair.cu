@@ -64,7 +64,11 @@ constexpr int kPOff = kBOff + kBStages * kBBytes;
 constexpr int kBarOff = kPOff + kPStages * kPBytes;
 constexpr int kNumBars = 2 * (kXStages + kPStages + kAccStages) + kBStages;
 static_assert(kXStages >= kBStages, "the done ring serves both the x and the B ring");
-constexpr int kSmemBytes = 1024 + kBarOff + 8 * kNumBars + 16;
+// Scatter epilogue: each epilogue warp stages 32 rows x 32 columns (bf16, 2 KB) here, so its NVLink
+// stores go out as 64-byte row pieces instead of one 16-byte piece per row.
+constexpr int kStgOff = (kBarOff + 8 * kNumBars + 64 + 127) / 128 * 128;
+constexpr int kStgBytes = 32 * 64;
+constexpr int kSmemBytes = 1024 + kStgOff + kEpiWarps * kStgBytes;
 constexpr int kTmemCols = 256 * kAccStages;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory plan");
 static_assert(kBOff % 1024 == 0 && kPOff % 1024 == 0, "stage alignment");
@@ -492,6 +496,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                             *reinterpret_cast<float4 *>(y + 8 * g8) = make_float4(o[0], o[1], o[2], o[3]);
                             *reinterpret_cast<float4 *>(y + 8 * g8 + 4) = make_float4(o[4], o[5], o[6], o[7]);
                         }
+                    } else if (a.scatter) {
+                        // Over NVLink: the warp's 32 rows x 32 columns go through shared memory (row pieces
+                        // of 64 bytes, 16-byte chunks swizzled by row pair so neither side conflicts), then
+                        // each store instruction writes 8 rows x 64 contiguous bytes.
+                        uint8_t *stg = smem + kStgOff + q * kStgBytes;
+#pragma unroll
+                        for (int g8 = 0; g8 < 4; ++g8) {
+                            uint32_t o[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e)
+                                o[e] = to16<F16>(__uint_as_float(v[8 * g8 + perm_pos(2 * e)])) |
+                                       (to16<F16>(__uint_as_float(v[8 * g8 + perm_pos(2 * e + 1)])) << 16);
+                            *reinterpret_cast<uint4 *>(stg + 64 * lane + 16 * (g8 ^ ((lane >> 1) & 3))) = make_uint4(o[0], o[1], o[2], o[3]);
+                        }
+                        __syncwarp();
+                        const int tok0 = tok - lane, c16 = lane & 3;
+#pragma unroll
+                        for (int s4 = 0; s4 < 4; ++s4) {
+                            const int r = 8 * s4 + (lane >> 2);
+                            const uint4 w = *reinterpret_cast<const uint4 *>(stg + 64 * r + 16 * (c16 ^ ((r >> 1) & 3)));
+                            if (tok0 + r < a.m) store_out16(a, par, tok0 + r, nb * 256 + 32 * cb + 8 * c16, w);
+                        }
+                        __syncwarp();
                     } else if (tok < a.m) {
 #pragma unroll
                         for (int g8 = 0; g8 < 4; ++g8) {
