@@ -64,10 +64,10 @@ constexpr int kPOff = kBOff + kBStages * kBBytes;
 constexpr int kBarOff = kPOff + kPStages * kPBytes;
 constexpr int kNumBars = 2 * (kXStages + kPStages + kAccStages) + kBStages;
 static_assert(kXStages >= kBStages, "the done ring serves both the x and the B ring");
-// Scatter epilogue: each epilogue warp stages 32 rows x 32 columns (bf16, 2 KB) here, so its NVLink
-// stores go out as 64-byte row pieces instead of one 16-byte piece per row.
+// Scatter epilogue: each epilogue warp stages 16 rows x 64 columns (bf16, 2 KB) at a time here, so its
+// NVLink stores go out as 128-byte row pieces instead of one 16-byte piece per row.
 constexpr int kStgOff = (kBarOff + 8 * kNumBars + 64 + 127) / 128 * 128;
-constexpr int kStgBytes = 32 * 64;
+constexpr int kStgBytes = 16 * 128;
 constexpr int kSmemBytes = 1024 + kStgOff + kEpiWarps * kStgBytes;
 constexpr int kTmemCols = 256 * kAccStages;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory plan");
@@ -200,7 +200,7 @@ __device__ __forceinline__ void split_epilogue(const PairArgs &a, uint32_t taddr
     }
 }
 
-template <bool F16, int EPI>
+template <bool F16, int EPI, bool SC = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ PairArgs a) {
     extern __shared__ uint8_t smem_raw[];
@@ -482,6 +482,46 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                 }
+            } else if constexpr (SC) {
+                // Over NVLink: 64 columns of the warp's 32 rows at a time, each half of the rows staged
+                // in shared memory (16 rows x 128 bytes, 16-byte chunks swizzled by row), then every
+                // store instruction writes 4 rows x 128 contiguous bytes.
+                uint8_t *stg = smem + kStgOff + q * kStgBytes;
+                const int tok0 = tok - lane;
+                for (int cp = 0; cp < 4; ++cp) {
+                    uint4 o[8];
+#pragma unroll
+                    for (int hv = 0; hv < 2; ++hv) {
+                        uint32_t v[32];
+                        tmem_ld32(taddr + 64 * cp + 32 * hv, v);
+#pragma unroll
+                        for (int g8 = 0; g8 < 4; ++g8) {
+                            uint32_t w[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e)
+                                w[e] = to16<F16>(__uint_as_float(v[8 * g8 + perm_pos(2 * e)])) |
+                                       (to16<F16>(__uint_as_float(v[8 * g8 + perm_pos(2 * e + 1)])) << 16);
+                            o[4 * hv + g8] = make_uint4(w[0], w[1], w[2], w[3]);
+                        }
+                    }
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {
+                        if ((lane >> 4) == half) {
+                            const int rl = lane & 15;
+#pragma unroll
+                            for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4 *>(stg + 128 * rl + 16 * (c ^ (rl & 7))) = o[c];
+                        }
+                        __syncwarp();
+#pragma unroll
+                        for (int s4 = 0; s4 < 4; ++s4) {
+                            const int rl = 4 * s4 + (lane >> 3), c = lane & 7;
+                            const uint4 w = *reinterpret_cast<const uint4 *>(stg + 128 * rl + 16 * (c ^ (rl & 7)));
+                            const int row = tok0 + 16 * half + rl;
+                            if (row < a.m) store_out16(a, par, row, nb * 256 + 64 * cp + 8 * c, w);
+                        }
+                        __syncwarp();
+                    }
+                }
             } else {
                 for (int cb = 0; cb < 8; ++cb) {
                     uint32_t v[32];
@@ -496,29 +536,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                             *reinterpret_cast<float4 *>(y + 8 * g8) = make_float4(o[0], o[1], o[2], o[3]);
                             *reinterpret_cast<float4 *>(y + 8 * g8 + 4) = make_float4(o[4], o[5], o[6], o[7]);
                         }
-                    } else if (a.scatter) {
-                        // Over NVLink: the warp's 32 rows x 32 columns go through shared memory (row pieces
-                        // of 64 bytes, 16-byte chunks swizzled by row pair so neither side conflicts), then
-                        // each store instruction writes 8 rows x 64 contiguous bytes.
-                        uint8_t *stg = smem + kStgOff + q * kStgBytes;
-#pragma unroll
-                        for (int g8 = 0; g8 < 4; ++g8) {
-                            uint32_t o[4];
-#pragma unroll
-                            for (int e = 0; e < 4; ++e)
-                                o[e] = to16<F16>(__uint_as_float(v[8 * g8 + perm_pos(2 * e)])) |
-                                       (to16<F16>(__uint_as_float(v[8 * g8 + perm_pos(2 * e + 1)])) << 16);
-                            *reinterpret_cast<uint4 *>(stg + 64 * lane + 16 * (g8 ^ ((lane >> 1) & 3))) = make_uint4(o[0], o[1], o[2], o[3]);
-                        }
-                        __syncwarp();
-                        const int tok0 = tok - lane, c16 = lane & 3;
-#pragma unroll
-                        for (int s4 = 0; s4 < 4; ++s4) {
-                            const int r = 8 * s4 + (lane >> 2);
-                            const uint4 w = *reinterpret_cast<const uint4 *>(stg + 64 * r + 16 * (c16 ^ ((r >> 1) & 3)));
-                            if (tok0 + r < a.m) store_out16(a, par, tok0 + r, nb * 256 + 32 * cb + 8 * c16, w);
-                        }
-                        __syncwarp();
                     } else if (tok < a.m) {
 #pragma unroll
                         for (int g8 = 0; g8 < 4; ++g8) {
@@ -550,9 +567,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-template <bool F16, int EPI>
+template <bool F16, int EPI, bool SC = false>
 int launch(const CUtensorMap &map, const PairArgs &a, cudaStream_t stream) {
-    auto kernel = gemm_pair_kernel<F16, EPI>;
+    auto kernel = gemm_pair_kernel<F16, EPI, SC>;
     static std::mutex mu;
     static bool configured[64] = {};
     int dev = 0;
@@ -657,6 +674,9 @@ void pair_band_order(int64_t m, int64_t k, int64_t n, int *band_rows, int *band)
 }
 
 int launch_gemm_pair(const CUtensorMap &map, const PairArgs &a, bool f16, int epilogue, cudaStream_t stream) {
+    // Scattering (HMB_EPI_STORE only): its own instantiation, so the staged NVLink epilogue adds no
+    // registers to the local kernels.
+    if (a.scatter) return f16 ? launch<true, HMB_EPI_STORE, true>(map, a, stream) : launch<false, HMB_EPI_STORE, true>(map, a, stream);
     if (f16) return epilogue == HMB_EPI_SWIGLU ? launch<true, HMB_EPI_SWIGLU>(map, a, stream) : launch<true, HMB_EPI_STORE>(map, a, stream);
     return epilogue == HMB_EPI_SWIGLU ? launch<false, HMB_EPI_SWIGLU>(map, a, stream) : launch<false, HMB_EPI_STORE>(map, a, stream);
 }
