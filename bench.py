@@ -80,6 +80,8 @@ def parse():
     ap.add_argument("--impl", default="hmb", choices=["hmb", "reference"])
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--cpu-sample-s", type=float, default=10.0)
+    ap.add_argument("--timeline", action="store_true",
+                    help="add the kernels of one profiled replay per rank to the line (diagnosis only)")
     ap.add_argument("--micro", default="", choices=["", "small", "small-once"],
                     help="instead of the stack: time the small kernels at 70B sizes (small-once: one launch each)")
     return ap.parse_args()
@@ -352,6 +354,8 @@ def run_hmb(args):
     }
     if decode_rec is not None:
         line["decode"] = decode_rec
+    if args.timeline and use_graph:
+        line["timeline"] = kernel_timeline(graph, barrier, world, dev)
     if rank == 0 and world == 1:
         line["cpu_baseline"] = cpu_baseline(wl, m, args.cpu_sample_s)
     torch.cuda.synchronize()
@@ -518,6 +522,31 @@ def end_to_end(stack, h0, m, args, flush, barrier, world, dev):
     nbytes = x_host.numel() * x_host.element_size()
     return {"value": round(m / (ms * 1e-3), 2), "unit": "tokens/s", "h2d_bytes_per_step": nbytes,
             "d2h_bytes_per_step": nbytes, "ms_per_step": round(ms, 5), "api": "FfnStack.forward_host"}
+
+
+def kernel_timeline(graph, barrier, world, dev):
+    """Diagnosis, not a measurement of the line: the kernels of one replay of the step's graph as
+    CUPTI records them under torch.profiler (name, start and duration in microseconds from the
+    replay's first kernel), on every rank; rank 0 gets all ranks' lists."""
+    import torch
+    import torch.distributed as dist
+    from torch.profiler import ProfilerActivity, profile
+
+    barrier()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        graph.replay()
+        torch.cuda.synchronize()
+    evs = sorted((ev.time_range.start, ev.time_range.end - ev.time_range.start,
+                  ev.name.replace("(anonymous namespace)::", "").split("(")[0][:80])
+                 for ev in prof.events() if ev.device_type == torch.autograd.DeviceType.CUDA)
+    t0 = evs[0][0] if evs else 0
+    mine = [(n, round(st - t0, 1), round(d, 1)) for st, d, n in evs]
+    barrier()
+    if world == 1:
+        return {"note": "profiled replay, diagnosis only", "ranks": [mine]}
+    every = [None] * world
+    dist.all_gather_object(every, mine)
+    return {"note": "profiled replay, diagnosis only", "ranks": every}
 
 
 def decode_record(stack, wl, args, barrier, world, dev, stream, hbm_gbs, peak_kind):
