@@ -68,9 +68,10 @@ static_assert(kXStages >= kBStages, "the done ring serves both the x and the B r
 // NVLink stores go out as 128-byte row pieces instead of one 16-byte piece per row.
 constexpr int kStgOff = (kBarOff + 8 * kNumBars + 64 + 127) / 128 * 128;
 constexpr int kStgBytes = 16 * 128;
-constexpr int kSmemBytes = 1024 + kStgOff + kEpiWarps * kStgBytes;
+constexpr int kSmemBytes = 1024 + kBarOff + 8 * kNumBars + 16;              // local output
+constexpr int kSmemBytesSc = 1024 + kStgOff + kEpiWarps * kStgBytes;         // scattering (SC)
 constexpr int kTmemCols = 256 * kAccStages;
-static_assert(kSmemBytes <= 227 * 1024, "shared memory plan");
+static_assert(kSmemBytes <= kSmemBytesSc && kSmemBytesSc <= 227 * 1024, "shared memory plan");
 static_assert(kBOff % 1024 == 0 && kPOff % 1024 == 0, "stage alignment");
 
 // 8 outputs (16 bytes) at column col of output row tok: into y, or over NVLink into the receive slots
@@ -570,6 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <bool F16, int EPI, bool SC = false>
 int launch(const CUtensorMap &map, const PairArgs &a, cudaStream_t stream) {
     auto kernel = gemm_pair_kernel<F16, EPI, SC>;
+    constexpr int kSmem = SC ? kSmemBytesSc : kSmemBytes;
     static std::mutex mu;
     static bool configured[64] = {};
     int dev = 0;
@@ -578,7 +580,7 @@ int launch(const CUtensorMap &map, const PairArgs &a, cudaStream_t stream) {
     {
         std::lock_guard<std::mutex> lock(mu);
         if (!configured[dev]) {
-            const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+            const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
             if (e != cudaSuccess) {
                 set_cuda_error(e);
                 return HMB_ERR_CUDA;
@@ -597,7 +599,7 @@ int launch(const CUtensorMap &map, const PairArgs &a, cudaStream_t stream) {
     attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.dynamicSmemBytes = kSmem;
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
