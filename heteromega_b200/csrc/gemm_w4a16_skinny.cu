@@ -34,7 +34,7 @@
 // Roles in a CTA of 15 warps:
 //   warp 0      TMA of the x tile [nt tokens x 64] of each step;
 //   warp 14     bulk copies of the block's two packed tiles of each K tile;
-//   warp 1      allocates TMEM (A stages at columns 0..127, two accumulators at 128..383); one thread
+//   warp 1      allocates TMEM (8 A stages at columns 0..255, two accumulators at 256..511); one thread
 //               issues tcgen05.mma (A from TMEM, M = 128, N = nt, K = 16) and commits each stage;
 //   warps 2-9   dequantize, two groups of four warps (one per TMEM lane quadrant), group h taking the
 //               64-row half h of every K tile: a lane reads 16 bytes of a packed tile (4 K rows x 8
@@ -67,7 +67,7 @@ constexpr int kStages = 8;                 // x ring, one stage per step
 constexpr int kPStages = 4;                // packed ring, one stage per K tile
 constexpr int kXBytes = kMaxNt * BK * 2;   // x tile of one step (nt rows used)
 constexpr int kPBytes = 2 * kTileBytes;    // the block's two packed tiles of one K tile
-constexpr int kAStages = 4, kAccStages = 2;
+constexpr int kAStages = 8, kAccStages = 2;
 constexpr int kACols = BK / 2;             // TMEM columns of one A stage: 64 K values as bf16 pairs
 constexpr int kAccCol0 = kAStages * kACols;
 constexpr int kTmemCols = 512;
