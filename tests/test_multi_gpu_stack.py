@@ -82,6 +82,7 @@ def _rank(rank, world, port, out_path):
             gen.manual_seed(7 + m)
             h0 = torch.randn(m, H_, device=dev, generator=gen).to(torch.bfloat16)
             got, ref = torch.empty_like(h0), torch.empty_like(h0)
+            st_tp.chain = True  # chained boundaries (taken at the two-shot sizes), checked below against unchained
             st_tp.forward(h0, got)
             graph, h_in, result = st_tp.graph(m)
             h_in.copy_(h0)
@@ -97,7 +98,6 @@ def _rank(rank, world, port, out_path):
             st_tp.chain = False
             unchained = torch.empty_like(h0)
             st_tp.forward(h0, unchained)
-            st_tp.chain = True
             torch.cuda.synchronize()
             res[f"chain_same{m}"] = np.array(bool(torch.equal(unchained, got)))
             mine = got.view(torch.int32).flatten()  # NCCL moves no 16-bit integers
